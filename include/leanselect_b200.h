@@ -1,0 +1,191 @@
+/*
+ * leanselect_b200.h -- C ABI of the B200 (sm_100a) LeanSelect prefill path.
+ *
+ * Four stages of LeanSelect's long-context prefill are exposed here:
+ *   key compression -> selector scoring (folded head mix) -> per-group top-T
+ *   page selection with forced sink/local pages -> block-sparse causal
+ *   attention over the selected 64-token pages.
+ *
+ * Conventions shared by every entry point
+ *   - All tensor pointers are DEVICE pointers on the current CUDA device;
+ *     bf16 tensors are passed as `uint16_t*` bit patterns.  Layouts are
+ *     row-major with the shapes given per argument.  cu_seqlens arrays are
+ *     int32 prefix sums of length batch+1 (the reference's varlen packing).
+ *   - Host scalars (batch, totals, maxima) are what the caller already knows;
+ *     the library never synchronises the stream to read device data.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call
+ *     is stream-ordered, stateless apart from cached tensor-map builders, and
+ *     reentrant across streams and threads.
+ *   - The caller allocates every buffer.  The library never allocates or
+ *     frees device memory on these paths.
+ *   - Return value: LS_OK or an LS_ERR_* code.  Argument and capability
+ *     checks happen on the host before anything is launched, so an error
+ *     return means nothing was enqueued.  `status` (nullable, device int32)
+ *     accumulates LS_DEVERR_* bits raised inside kernels (bad indices, a
+ *     bounded wait that expired); kernels never trap.
+ *
+ * Reference interfaces (paths relative to the LeanSelect repository).
+ */
+#ifndef LEANSELECT_B200_H_
+#define LEANSELECT_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Host-side return codes. */
+#define LS_OK 0
+#define LS_ERR_INVALID_ARGUMENT 1 /* null pointer, bad shape, inconsistent sizes */
+#define LS_ERR_UNSUPPORTED 2      /* valid but not compiled (e.g. head_dim != 128) */
+#define LS_ERR_ALIGNMENT 3        /* a pointer or stride is not 16-byte aligned */
+#define LS_ERR_CUDA 4             /* a CUDA runtime/driver call failed */
+
+/* Device-side status bits (OR-ed into *status). */
+#define LS_DEVERR_TIMEOUT 0x1          /* a bounded wait expired; outputs are invalid */
+#define LS_DEVERR_PAGE_INDEX 0x2       /* a topk_idx entry >= number of key pages (ignored) */
+#define LS_DEVERR_SEQLENS 0x4          /* cu_seqlens not monotone or beyond the totals */
+
+/* Largest per-row page budget T accepted by ls_select_pages/ls_sparse_attn. */
+#define LS_MAX_TOPK 128
+
+/* Human-readable name of an LS_ERR_* code. */
+const char* ls_status_string(int code);
+
+/* Text of the last host-side error raised on the calling thread. */
+const char* ls_last_error(void);
+
+/* Library build identity: "leanselect_b200 <version> sm_100a". */
+const char* ls_version(void);
+
+/*
+ * ls_fold_weights -- replaces LeanSelectSelector.fused_weights
+ * (leanselect/selector.py:144-158).
+ *
+ * q_fused[h, d, rho*r + j]  = head_mix[h, rho]    * q_proj[rho, d, j]
+ * kv_fused[g, d, rho*r + j] = kv_head_mix[g, rho] * k_proj[rho, d, j]
+ * Inputs are fp32 (the selector is kept in fp32, models/__init__.py:178-181).
+ * Outputs (each nullable):
+ *   q_fused_f32 [H, D, F], kv_fused_f32 [G, D, F]   fp32, reference layout
+ *   q_fused_bf16 [H, D, F], kv_fused_bf16 [G, D, F] bf16, reference layout
+ *   wq_t [G, F, Hg*D], wk_t [G, F, D]               bf16, kernel (K-major) layout
+ * with F = R*r and Hg = H/G.
+ */
+int ls_fold_weights(const float* head_mix, const float* kv_head_mix, const float* q_proj,
+                    const float* k_proj, int32_t num_heads, int32_t num_kv_heads,
+                    int32_t head_dim, int32_t router_heads, int32_t router_dim,
+                    float* q_fused_f32, float* kv_fused_f32, uint16_t* q_fused_bf16,
+                    uint16_t* kv_fused_bf16, uint16_t* wq_t, uint16_t* wk_t, void* stream);
+
+/*
+ * ls_compressed_seqlens -- replaces the cu_seqlens_compressed half of
+ * calc_chunks_with_stride (leanselect/models/minicpm.py:710-750).
+ * cu_seqlens_c[b+1] = cu_seqlens_c[b] + (n_b >= kernel_size ? (n_b - kernel_size)/kernel_stride + 1 : 0).
+ */
+int ls_compressed_seqlens(const int32_t* cu_seqlens_k, int32_t batch, int32_t kernel_size,
+                          int32_t kernel_stride, int32_t* cu_seqlens_c, int32_t* status,
+                          void* stream);
+
+/*
+ * ls_compress_keys -- replaces CompressK.forward (leanselect/models/minicpm.py:1169-1185)
+ * (same math as pages.compress_keys_mean, leanselect/pages.py:84-101).
+ *
+ * k [total_k, G, D] bf16 -> k_compressed [total_c, G, D] bf16 and
+ * cu_seqlens_c [batch+1].  Atom i of sequence b is the mean of keys
+ * [16 i, 16 i + 32) of that sequence (kernel_size/kernel_stride in general,
+ * kernel_size a multiple of kernel_stride).  total_c must equal the value
+ * implied by cu_seqlens_k (the caller computes it, as the reference does on
+ * the host); G*D must be a multiple of 8 and at most 2048.
+ */
+int ls_compress_keys(const uint16_t* k, const int32_t* cu_seqlens_k, int32_t batch,
+                     int64_t total_k, int32_t num_kv_heads, int32_t head_dim,
+                     int32_t kernel_size, int32_t kernel_stride, uint16_t* k_compressed,
+                     int32_t* cu_seqlens_c, int64_t total_c, int32_t* status, void* stream);
+
+/*
+ * ls_project_atom_keys -- replaces LeanSelectSelector.project_atom_keys
+ * (leanselect/selector.py:179-190).
+ * kc [total_c, G, D] bf16, wk_t [G, F, D] bf16 -> ks [G, total_c, F] bf16
+ * (fp32 accumulation, one rounding to bf16 as the reference's bf16 einsum).
+ */
+int ls_project_atom_keys(const uint16_t* kc, int64_t total_c, int32_t num_kv_heads,
+                         int32_t head_dim, const uint16_t* wk_t, int32_t width, uint16_t* ks,
+                         void* stream);
+
+/*
+ * ls_project_queries -- replaces LeanSelectSelector.project_queries
+ * (leanselect/selector.py:160-177); tcgen05 GEMM.
+ * q [total_q, H, D] bf16, wq_t [G, F, Hg*D] bf16 -> qs [G, total_q, F] bf16.
+ * Requires D == 128, F == 128, Hg in {8, 16}.
+ */
+int ls_project_queries(const uint16_t* q, int64_t total_q, int32_t num_heads,
+                       int32_t num_kv_heads, int32_t head_dim, const uint16_t* wq_t,
+                       int32_t width, uint16_t* qs, int32_t* status, void* stream);
+
+/*
+ * ls_score_pages -- replaces LeanSelectSelector.score_pages
+ * (leanselect/selector.py:192-214) with pool_atoms_to_pages(reduce="max")
+ * (leanselect/pages.py:146-187), for a packed batch.
+ *
+ * Page scores [G, total_q, max_pages] fp32, max_pages = ceil(max_seqlen_q/block):
+ * row t of sequence b holds the max over atoms [4p-1, 4p+4) of Qs[t]·Ks[a]
+ * for p < P_b (no causal mask, as the reference) and -inf for p >= P_b.
+ * q is the post-RoPE query; ks comes from ls_project_atom_keys.  Requires
+ * block_size == 64, kernel_stride == 16.
+ */
+int ls_score_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                   const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_c, int32_t batch,
+                   int32_t max_seqlen_q, int64_t total_q, int64_t total_c, int32_t num_heads,
+                   int32_t num_kv_heads, int32_t head_dim, int32_t width, int32_t block_size,
+                   int32_t kernel_stride, float* page_scores, int32_t* status, void* stream);
+
+/*
+ * ls_select_pages -- replaces the selection loop of
+ * MiniCPMInfLLMv2Attention._lightweight_compressed_attention
+ * (leanselect/models/minicpm.py:3093-3141): fused Q projection, atom scoring,
+ * page pooling, visibility/forced masking and streaming top-T in one
+ * tcgen05 kernel.  Page scores are never written to HBM.
+ *
+ * topk_idx [G, total_q, take] int32, take = min(topk, max_pages) as in the
+ * reference (minicpm.py:3096-3104).  Row t of sequence b holds the forced
+ * pages (p < init_blocks, and p in [t/64 - local_blocks, t/64]) followed by
+ * the best-scoring visible non-forced pages, min(take, P_b) entries in all,
+ * then -1.  Order within a row is unspecified (the reference uses
+ * torch.topk(sorted=False)); ties are broken toward the lower page index.
+ * Requires take <= LS_MAX_TOPK, block_size == 64, kernel_stride == 16.
+ */
+int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                    const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_c, int32_t batch,
+                    int32_t max_seqlen_q, int64_t total_q, int64_t total_c, int32_t num_heads,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t width, int32_t take,
+                    int32_t init_blocks, int32_t local_blocks, int32_t block_size,
+                    int32_t kernel_stride, int32_t* topk_idx, int32_t* status, void* stream);
+
+/*
+ * ls_sparse_attn -- replaces infllmv2_attn_varlen_func(..., topk_idx=)
+ * (called at leanselect/models/minicpm.py:3229-3243; InfLLM-v2 varlen_fwd
+ * with a block mask, third_party/infllmv2/paper1.patch).
+ *
+ * For packed query t of sequence b and head h (group g = h / (H/G)):
+ *   out[t, h] = softmax_k(scale * q[t,h]·k[k,g]) v[k,g]
+ * over keys k of sequence b lying in a page listed in topk_idx[g, t, :]
+ * (entries < 0 are empty, duplicates count once) and, with causal != 0, at
+ * relative position <= t_rel + (N_k - N_q).  Rows with no key output zeros
+ * (lse = +inf).  q [total_q, H, D], k/v [total_k, G, D], out [total_q, H, D]
+ * bf16; lse [H, total_q] fp32 (nullable); scale <= 0 selects D^-0.5.
+ * Requires D == 128, H/G in {8, 16}, block_size == 64, topk <= LS_MAX_TOPK.
+ */
+int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                   const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t batch,
+                   int32_t max_seqlen_q, int32_t max_seqlen_k, int64_t total_q, int64_t total_k,
+                   int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                   const int32_t* topk_idx, int32_t topk, int32_t block_size,
+                   float softmax_scale, int32_t causal, uint16_t* out, float* lse,
+                   int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LEANSELECT_B200_H_ */

@@ -1,0 +1,84 @@
+// Internal launcher declarations shared by the kernels and the C ABI layer.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace ls {
+
+cudaError_t launch_fold_weights(const float* head_mix, const float* kv_head_mix,
+                                const float* q_proj, const float* k_proj, int H, int G, int D,
+                                int R, int r, float* q_f32, float* kv_f32, uint16_t* q_bf16,
+                                uint16_t* kv_bf16, uint16_t* wq_t, uint16_t* wk_t,
+                                cudaStream_t stream);
+
+cudaError_t launch_compressed_seqlens(const int32_t* cu_k, int batch, int kernel_size,
+                                      int kernel_stride, int32_t* cu_c, int32_t* status,
+                                      cudaStream_t stream);
+
+cudaError_t launch_compress_keys(const uint16_t* k, const int32_t* cu_k, const int32_t* cu_c,
+                                 int batch, int64_t total_k, int64_t total_c, int G, int D,
+                                 int kernel_size, int kernel_stride, uint16_t* kc,
+                                 int32_t* status, cudaStream_t stream);
+
+cudaError_t launch_project_atom_keys(const uint16_t* kc, int64_t total_c, int G,
+                                     const uint16_t* wk_t, uint16_t* ks, cudaStream_t stream);
+
+// Score/select kernel family (score_select.cu).
+enum ScoreMode { kModeProject = 0, kModeScore = 1, kModeSelect = 2 };
+
+struct ScoreArgs {
+  CUtensorMap tm_q;    // Q as [total_q, H*D] bf16, box {64, 128}, 128B swizzle
+  CUtensorMap tm_w;    // WqT as [G*F, Hg*D] bf16, box {64, 128}
+  CUtensorMap tm_ks;   // Ks as [G*total_c, F] bf16, box {64, 128}
+  const int32_t* cu_q;
+  const int32_t* cu_c;
+  int batch;
+  int num_groups;
+  int hg;              // query heads per group
+  int max_seqlen_q;
+  int64_t total_q;
+  int64_t total_c;
+  int take;            // output width of topk_idx
+  int init_blocks;
+  int local_blocks;
+  int max_pages;       // ceil(max_seqlen_q / 64): width of page_scores
+  int32_t* topk_idx;   // kModeSelect
+  float* page_scores;  // kModeScore
+  uint16_t* qs_out;    // kModeProject: [G, total_q, F] bf16
+  int32_t* status;
+};
+
+cudaError_t launch_score(int mode, const ScoreArgs& args, cudaStream_t stream);
+
+// Sparse attention (sparse_attn.cu).
+struct AttnArgs {
+  CUtensorMap tm_k;    // K as [total_k, G*D] bf16, box {64, 64}, 128B swizzle
+  CUtensorMap tm_v;    // V, same geometry
+  const uint16_t* q;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  const int32_t* topk_idx;
+  int batch;
+  int num_heads;
+  int num_groups;
+  int topk;
+  int causal;
+  float scale_log2;    // softmax_scale * log2(e)
+  float scale;         // softmax_scale
+  int64_t total_q;
+  int64_t total_k;
+  uint16_t* out;
+  float* lse;
+  int32_t* status;
+};
+
+cudaError_t launch_sparse_attn(const AttnArgs& args, cudaStream_t stream);
+
+// Builds a 2-D bf16 tensor map (row-major [rows, cols], 128B swizzle).
+// Returns false if the driver entry point is unavailable or encoding fails.
+bool make_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                        uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows);
+
+}  // namespace ls

@@ -1,0 +1,339 @@
+// Streaming kernels of the selection path: selector weight folding, the
+// compressed cu_seqlens, key compression (a1) and the atom-key projection (a4).
+//
+// These are HBM- or launch-bound SIMT kernels; the GEMM-shaped work lives in
+// score_select.cu.
+#include "common.cuh"
+#include "launch.h"
+
+#include <algorithm>
+
+namespace ls {
+
+// ---------------------------------------------------------------------------
+// Weight folding (selector.py:144-158)
+// ---------------------------------------------------------------------------
+
+__global__ void fold_weights_kernel(const float* __restrict__ head_mix,
+                                    const float* __restrict__ kv_head_mix,
+                                    const float* __restrict__ q_proj,
+                                    const float* __restrict__ k_proj, int H, int G, int D, int R,
+                                    int r, float* q_f32, float* kv_f32, __nv_bfloat16* q_bf16,
+                                    __nv_bfloat16* kv_bf16, __nv_bfloat16* wq_t,
+                                    __nv_bfloat16* wk_t) {
+  const int F = R * r;
+  const int Hg = H / G;
+  const int64_t nq = static_cast<int64_t>(H) * D * F;
+  const int64_t nk = static_cast<int64_t>(G) * D * F;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nq + nk;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (i < nq) {
+      // q_fused[h, d, f], f = rho * r + j
+      const int f = static_cast<int>(i % F);
+      const int d = static_cast<int>((i / F) % D);
+      const int h = static_cast<int>(i / (static_cast<int64_t>(F) * D));
+      const int rho = f / r, j = f % r;
+      const float w = head_mix[h * R + rho] * q_proj[(static_cast<int64_t>(rho) * D + d) * r + j];
+      if (q_f32) q_f32[i] = w;
+      const __nv_bfloat16 wb = __float2bfloat16_rn(w);
+      if (q_bf16) q_bf16[i] = wb;
+      if (wq_t) {
+        const int g = h / Hg, s = h % Hg;
+        wq_t[(static_cast<int64_t>(g) * F + f) * (Hg * D) + s * D + d] = wb;
+      }
+    } else {
+      const int64_t k = i - nq;
+      const int f = static_cast<int>(k % F);
+      const int d = static_cast<int>((k / F) % D);
+      const int g = static_cast<int>(k / (static_cast<int64_t>(F) * D));
+      const int rho = f / r, j = f % r;
+      const float w =
+          kv_head_mix[g * R + rho] * k_proj[(static_cast<int64_t>(rho) * D + d) * r + j];
+      if (kv_f32) kv_f32[k] = w;
+      const __nv_bfloat16 wb = __float2bfloat16_rn(w);
+      if (kv_bf16) kv_bf16[k] = wb;
+      if (wk_t) wk_t[(static_cast<int64_t>(g) * F + f) * D + d] = wb;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Compressed cu_seqlens (minicpm.py:710-750)
+// ---------------------------------------------------------------------------
+
+__global__ void compressed_seqlens_kernel(const int32_t* __restrict__ cu_k, int batch,
+                                          int kernel_size, int kernel_stride,
+                                          int32_t* __restrict__ cu_c, int32_t* status) {
+  __shared__ int32_t warp_sums[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) {
+    carry = 0;
+    cu_c[0] = 0;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int base = 0; base < batch; base += blockDim.x) {
+    const int b = base + threadIdx.x;
+    int32_t count = 0;
+    if (b < batch) {
+      const int32_t n = cu_k[b + 1] - cu_k[b];
+      if (n < 0) report(status, LS_DEVERR_SEQLENS);
+      count = n >= kernel_size ? (n - kernel_size) / kernel_stride + 1 : 0;
+    }
+    int32_t incl = count;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      const int nw = blockDim.x >> 5;
+      int32_t w = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t v = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += v;
+      }
+      if (lane < nw) warp_sums[lane] = w;
+    }
+    __syncthreads();
+    const int32_t prefix = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl;
+    if (b < batch) cu_c[b + 1] = prefix;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = prefix;
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Key compression (CompressK.forward, minicpm.py:1169-1185)
+// ---------------------------------------------------------------------------
+//
+// One thread owns one 16-byte vector (8 channels) of the [G*D] row and a chunk
+// of kChunk consecutive packed atoms.  It streams the keys once: run sums of
+// `stride` tokens are kept in registers and atom i is the ordered sum of runs
+// i .. i+R-1 (R = kernel_size / stride), times 1/kernel_size, rounded to bf16.
+// The order of the fp32 additions is the oracle's, so results match it
+// bit for bit.  A warp covers one 512-byte key row for G*D = 256.
+
+constexpr int kCompressChunk = 8;
+
+template <int R>
+__global__ void compress_keys_kernel(const uint4* __restrict__ k, const int32_t* __restrict__ cu_k,
+                                     const int32_t* __restrict__ cu_c, int batch, int64_t total_k,
+                                     int64_t total_c, int vecs_per_row, int stride,
+                                     float inv_kernel, uint4* __restrict__ kc, int32_t* status) {
+  const int chunks_per_block = blockDim.x / vecs_per_row;
+  const int local_chunk = threadIdx.x / vecs_per_row;
+  const int vec = threadIdx.x % vecs_per_row;
+  if (local_chunk >= chunks_per_block) return;
+  const int64_t chunk = static_cast<int64_t>(blockIdx.x) * chunks_per_block + local_chunk;
+  int64_t atom = chunk * kCompressChunk;
+  if (atom >= total_c) return;
+  const int64_t atom_end = min(atom + kCompressChunk, total_c);
+
+  int b = find_sequence(cu_c, batch, atom);
+  while (atom < atom_end) {
+    // Skip sequences without atoms (cu_c[b] == cu_c[b+1]).
+    while (b < batch - 1 && static_cast<int64_t>(__ldg(cu_c + b + 1)) <= atom) ++b;
+    const int64_t seq_atom_end = ::min(atom_end, static_cast<int64_t>(__ldg(cu_c + b + 1)));
+    const int64_t local = atom - __ldg(cu_c + b);
+    const int64_t tok0 = __ldg(cu_k + b) + local * stride;
+    if (tok0 + (seq_atom_end - atom - 1 + R) * stride > total_k) {
+      report(status, LS_DEVERR_SEQLENS);
+      return;
+    }
+    float run[R][8];
+    // Runs local .. local+R-2 precede the first atom's last run.
+#pragma unroll
+    for (int j = 0; j < R - 1; ++j) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) run[j + 1][c] = 0.f;
+      const uint4* src = k + (tok0 + static_cast<int64_t>(j) * stride) * vecs_per_row + vec;
+      for (int t = 0; t < stride; ++t) {
+        const uint4 u = __ldg(src + static_cast<int64_t>(t) * vecs_per_row);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float2 f = __bfloat1622float2(h[c]);
+          run[j + 1][2 * c] += f.x;
+          run[j + 1][2 * c + 1] += f.y;
+        }
+      }
+    }
+    for (int64_t a = atom; a < seq_atom_end; ++a) {
+      // Shift the window: runs[0..R-2] <- runs[1..R-1], then load run R-1.
+#pragma unroll
+      for (int j = 0; j < R - 1; ++j)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) run[j][c] = run[j + 1][c];
+      float nr[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) nr[c] = 0.f;
+      const int64_t t0 = tok0 + (a - atom + R - 1) * stride;
+      const uint4* src = k + t0 * vecs_per_row + vec;
+      for (int t = 0; t < stride; ++t) {
+        const uint4 u = __ldg(src + static_cast<int64_t>(t) * vecs_per_row);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float2 f = __bfloat1622float2(h[c]);
+          nr[2 * c] += f.x;
+          nr[2 * c + 1] += f.y;
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) run[R - 1][c] = nr[c];
+      float acc[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        acc[c] = 0.f;
+#pragma unroll
+        for (int j = 0; j < R; ++j) acc[c] += run[j][c];
+        acc[c] *= inv_kernel;
+      }
+      uint4 out;
+      out.x = pack_bf16x2(acc[0], acc[1]);
+      out.y = pack_bf16x2(acc[2], acc[3]);
+      out.z = pack_bf16x2(acc[4], acc[5]);
+      out.w = pack_bf16x2(acc[6], acc[7]);
+      kc[a * vecs_per_row + vec] = out;
+    }
+    atom = seq_atom_end;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Atom-key projection (selector.py:179-190): Ks[g, a, f] = sum_d Kc[a, g, d] Wk[g, f, d]
+// ---------------------------------------------------------------------------
+
+constexpr int kProjAtoms = 32;
+
+__global__ void __launch_bounds__(256) project_atom_keys_kernel(
+    const __nv_bfloat16* __restrict__ kc, int64_t total_c, int G, const __nv_bfloat16* __restrict__ wk_t,
+    __nv_bfloat16* __restrict__ ks) {
+  // D = F = 128.  Padded rows keep the 16-byte reads of W conflict-free.
+  constexpr int D = 128, F = 128, WP = D + 8;
+  __shared__ __align__(16) __nv_bfloat16 w_s[F * WP];
+  __shared__ __align__(16) __nv_bfloat16 k_s[kProjAtoms * D];
+  const int g = blockIdx.y;
+  const int64_t a0 = static_cast<int64_t>(blockIdx.x) * kProjAtoms;
+  for (int i = threadIdx.x; i < F * D / 8; i += blockDim.x) {
+    const int f = i / (D / 8), c = i % (D / 8);
+    *reinterpret_cast<uint4*>(&w_s[f * WP + c * 8]) =
+        *reinterpret_cast<const uint4*>(&wk_t[(static_cast<int64_t>(g) * F + f) * D + c * 8]);
+  }
+  for (int i = threadIdx.x; i < kProjAtoms * D / 8; i += blockDim.x) {
+    const int a = i / (D / 8), c = i % (D / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (a0 + a < total_c)
+      v = *reinterpret_cast<const uint4*>(&kc[((a0 + a) * G + g) * D + c * 8]);
+    *reinterpret_cast<uint4*>(&k_s[a * D + c * 8]) = v;
+  }
+  __syncthreads();
+  const int f = threadIdx.x & (F - 1);
+  const int abase = (threadIdx.x >> 7) * (kProjAtoms / 2);
+  float acc[kProjAtoms / 2];
+#pragma unroll
+  for (int i = 0; i < kProjAtoms / 2; ++i) acc[i] = 0.f;
+  for (int d = 0; d < D; d += 8) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(&w_s[f * WP + d]);
+    const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wv);
+    float w[8];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float2 t = __bfloat1622float2(wh[c]);
+      w[2 * c] = t.x;
+      w[2 * c + 1] = t.y;
+    }
+#pragma unroll
+    for (int i = 0; i < kProjAtoms / 2; ++i) {
+      const uint4 kv = *reinterpret_cast<const uint4*>(&k_s[(abase + i) * D + d]);
+      const __nv_bfloat162* kh = reinterpret_cast<const __nv_bfloat162*>(&kv);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float2 t = __bfloat1622float2(kh[c]);
+        acc[i] = fmaf(t.x, w[2 * c], acc[i]);
+        acc[i] = fmaf(t.y, w[2 * c + 1], acc[i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kProjAtoms / 2; ++i) {
+    const int64_t a = a0 + abase + i;
+    if (a < total_c) ks[(static_cast<int64_t>(g) * total_c + a) * F + f] = __float2bfloat16_rn(acc[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+
+cudaError_t launch_fold_weights(const float* head_mix, const float* kv_head_mix,
+                                const float* q_proj, const float* k_proj, int H, int G, int D,
+                                int R, int r, float* q_f32, float* kv_f32, uint16_t* q_bf16,
+                                uint16_t* kv_bf16, uint16_t* wq_t, uint16_t* wk_t,
+                                cudaStream_t stream) {
+  const int64_t n = static_cast<int64_t>(H + G) * D * R * r;
+  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
+  fold_weights_kernel<<<blocks, 256, 0, stream>>>(
+      head_mix, kv_head_mix, q_proj, k_proj, H, G, D, R, r, q_f32, kv_f32,
+      reinterpret_cast<__nv_bfloat16*>(q_bf16), reinterpret_cast<__nv_bfloat16*>(kv_bf16),
+      reinterpret_cast<__nv_bfloat16*>(wq_t), reinterpret_cast<__nv_bfloat16*>(wk_t));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_compressed_seqlens(const int32_t* cu_k, int batch, int kernel_size,
+                                      int kernel_stride, int32_t* cu_c, int32_t* status,
+                                      cudaStream_t stream) {
+  compressed_seqlens_kernel<<<1, 1024, 0, stream>>>(cu_k, batch, kernel_size, kernel_stride,
+                                                     cu_c, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_compress_keys(const uint16_t* k, const int32_t* cu_k, const int32_t* cu_c,
+                                 int batch, int64_t total_k, int64_t total_c, int G, int D,
+                                 int kernel_size, int kernel_stride, uint16_t* kc,
+                                 int32_t* status, cudaStream_t stream) {
+  if (total_c == 0) return cudaSuccess;
+  const int vecs = G * D / 8;
+  const int chunks_per_block = vecs >= 256 ? 1 : 256 / vecs;
+  const int threads = vecs >= 256 ? vecs : chunks_per_block * vecs;
+  const int64_t chunks = (total_c + kCompressChunk - 1) / kCompressChunk;
+  const int64_t blocks = (chunks + chunks_per_block - 1) / chunks_per_block;
+  const float inv = 1.0f / static_cast<float>(kernel_size);
+  const int R = kernel_size / kernel_stride;
+  const uint4* kv = reinterpret_cast<const uint4*>(k);
+  uint4* out = reinterpret_cast<uint4*>(kc);
+  switch (R) {
+    case 1:
+      compress_keys_kernel<1><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+          kv, cu_k, cu_c, batch, total_k, total_c, vecs, kernel_stride, inv, out, status);
+      break;
+    case 2:
+      compress_keys_kernel<2><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+          kv, cu_k, cu_c, batch, total_k, total_c, vecs, kernel_stride, inv, out, status);
+      break;
+    case 4:
+      compress_keys_kernel<4><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+          kv, cu_k, cu_c, batch, total_k, total_c, vecs, kernel_stride, inv, out, status);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_project_atom_keys(const uint16_t* kc, int64_t total_c, int G,
+                                     const uint16_t* wk_t, uint16_t* ks, cudaStream_t stream) {
+  if (total_c == 0) return cudaSuccess;
+  dim3 grid(static_cast<unsigned>((total_c + kProjAtoms - 1) / kProjAtoms), G);
+  project_atom_keys_kernel<<<grid, 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(kc), total_c, G,
+      reinterpret_cast<const __nv_bfloat16*>(wk_t), reinterpret_cast<__nv_bfloat16*>(ks));
+  return cudaGetLastError();
+}
+
+}  // namespace ls

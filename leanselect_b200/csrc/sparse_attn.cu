@@ -1,0 +1,429 @@
+// Block-sparse causal attention over per-token page lists (stage 2, a9).
+//
+// Replaces infllmv2_attn_varlen_func(..., topk_idx=) (minicpm.py:3229-3243).
+// LeanSelect picks pages per query token, and on the benchmark inputs the
+// lists of neighbouring tokens barely overlap, so a tensor-core tile that
+// spans several tokens would compute mostly masked products.  This kernel
+// therefore works per (token, KV group): the Hg query heads of the group form
+// the 16 rows of an m16n8k16 tile and the keys of the token's own pages form
+// the columns, so every product computed is a product the token needs.
+//
+// CTA = one (packed token, group); 5 warps:
+//   warp 4      TMA producer: streams each selected page's K and V
+//               (64 keys x 128 dims each, two 128B-swizzled boxes apiece)
+//               through a 3-stage shared-memory ring (32 KB per stage);
+//   warps 0..3  consumers: warp w owns keys 16w..16w+15 of every page and
+//               keeps its own online softmax (m, l, O[16 x 128] in registers);
+//               the four partial results are merged at the end.
+// The page list is loaded once, invalid entries dropped, sorted and
+// de-duplicated by one warp (bitonic network over 128 slots).
+#include "common.cuh"
+#include "launch.h"
+
+namespace ls {
+namespace {
+
+constexpr int kStages = 3;
+constexpr int kBoxBytes = 64 * 128;            // 64 keys x 64 dims bf16
+constexpr int kStageBytes = 4 * kBoxBytes;     // K half0, K half1, V half0, V half1
+constexpr int kThreads = 160;
+constexpr int kMaxT = LS_MAX_TOPK;
+constexpr int32_t kSentinel = 0x7FFFFFFF;
+
+struct AttnSmem {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  int abort_flag;
+  int n_pages;
+  int32_t pages[kMaxT];
+  float m_part[4][16];
+  float l_part[4][16];
+};
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                          uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Byte offset of 16-byte chunk `chunk` (0..7) of row `row` in a 128B-swizzled box.
+__device__ __forceinline__ uint32_t sw128(int row, int chunk) {
+  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// Sorts 128 keys held as v[r] at position 32*r + lane, ascending.
+__device__ __forceinline__ void warp_bitonic_sort128(int32_t (&v)[4], int lane) {
+#pragma unroll
+  for (int k = 2; k <= 128; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= 32) {
+        const int rj = j >> 5;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          if ((r & rj) == 0) {
+            const int pos = 32 * r + lane;
+            const bool up = (pos & k) == 0;
+            const int32_t a = v[r], b = v[r | rj];
+            const bool swap = up ? (a > b) : (a < b);
+            v[r] = swap ? b : a;
+            v[r | rj] = swap ? a : b;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int pos = 32 * r + lane;
+          const int32_t other = __shfl_xor_sync(0xffffffffu, v[r], j);
+          const bool up = (pos & k) == 0;
+          const bool lower = (lane & j) == 0;
+          const int32_t lo = min(v[r], other), hi = max(v[r], other);
+          v[r] = (lower == up) ? lo : hi;
+        }
+      }
+    }
+  }
+}
+
+template <int HG>
+__global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_constant__ AttnArgs args) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* stages = smem;
+  uint8_t* q_smem = stages + kStages * kStageBytes;  // [16 rows x 256 B], swizzled chunks
+  AttnSmem* sm = reinterpret_cast<AttnSmem*>(q_smem + 16 * 256);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = args.num_groups;
+  const int64_t t = blockIdx.x / G;
+  const int g = static_cast<int>(blockIdx.x % G);
+  const int b = find_sequence(args.cu_q, args.batch, t);
+  const int64_t q_start = __ldg(args.cu_q + b);
+  const int64_t k_start = __ldg(args.cu_k + b);
+  const int nq = static_cast<int>(__ldg(args.cu_q + b + 1) - q_start);
+  const int nk = static_cast<int>(__ldg(args.cu_k + b + 1) - k_start);
+  const int t_rel = static_cast<int>(t - q_start);
+  const int t_lim = args.causal ? min(nk - 1, t_rel + (nk - nq)) : nk - 1;
+  const int n_kpages = (nk + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm->full[s], 1);
+      mbar_init(&sm->empty[s], 4);
+    }
+    sm->abort_flag = 0;
+    fence_barrier_init();
+  }
+
+  if (warp == 0) {
+    // Page list: drop empty/out-of-range/fully-masked entries, sort, de-duplicate.
+    int32_t v[4];
+    const int32_t* row = args.topk_idx + (static_cast<int64_t>(g) * args.total_q + t) * args.topk;
+    bool bad_index = false;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int pos = 32 * r + lane;
+      int32_t p = pos < args.topk ? __ldg(row + pos) : -1;
+      if (p >= n_kpages) bad_index = true;
+      v[r] = (p >= 0 && p < n_kpages && p * 64 <= t_lim) ? p : kSentinel;
+    }
+    if (__any_sync(0xffffffffu, bad_index) && lane == 0) report(args.status, LS_DEVERR_PAGE_INDEX);
+    warp_bitonic_sort128(v, lane);
+    int base = 0;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      int32_t prev = __shfl_up_sync(0xffffffffu, v[r], 1);
+      const int32_t prev_reg = r > 0 ? __shfl_sync(0xffffffffu, v[r - 1], 31) : -1;
+      if (lane == 0) prev = prev_reg;
+      const bool keep = v[r] != kSentinel && v[r] != prev;
+      const uint32_t mask = __ballot_sync(0xffffffffu, keep);
+      if (keep) sm->pages[base + __popc(mask & ((1u << lane) - 1))] = v[r];
+      base += __popc(mask);
+    }
+    if (lane == 0) sm->n_pages = base;
+  } else if (warp == 1) {
+    // Q rows of this group (HG heads, padded to 16 rows with zeros), swizzled.
+    const uint4* src = reinterpret_cast<const uint4*>(args.q + (t * args.num_heads + g * HG) * 128);
+    for (int i = lane; i < 16 * 16; i += 32) {
+      const int r = i >> 4, c = i & 15;
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (r < HG) val = __ldg(src + r * 16 + c);
+      *reinterpret_cast<uint4*>(q_smem + r * 256 + (((c & 7) ^ (r & 7)) | (c & 8)) * 16) = val;
+    }
+  }
+  __syncthreads();
+  const int n_pages = sm->n_pages;
+  volatile int* abort_flag = &sm->abort_flag;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      tma_prefetch_desc(&args.tm_k);
+      tma_prefetch_desc(&args.tm_v);
+      int i = 0;
+      bool ok = true;
+      for (; i < n_pages; ++i) {
+        const int s = i % kStages;
+        ok = mbar_wait(&sm->empty[s], ((i / kStages) & 1) ^ 1, args.status, abort_flag);
+        if (!ok) break;
+        uint8_t* st = stages + s * kStageBytes;
+        const int32_t y = static_cast<int32_t>(k_start + static_cast<int64_t>(sm->pages[i]) * 64);
+        const int32_t x = g * 128;
+        mbar_arrive_expect_tx(&sm->full[s], kStageBytes);
+        tma_load_2d(st, &args.tm_k, &sm->full[s], x, y);
+        tma_load_2d(st + kBoxBytes, &args.tm_k, &sm->full[s], x + 64, y);
+        tma_load_2d(st + 2 * kBoxBytes, &args.tm_v, &sm->full[s], x, y);
+        tma_load_2d(st + 3 * kBoxBytes, &args.tm_v, &sm->full[s], x + 64, y);
+      }
+      if (!ok) {
+        for (int k = max(0, i - kStages); k < i; ++k)
+          mbar_wait(&sm->full[k % kStages], (k / kStages) & 1, nullptr, nullptr);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
+  // Q fragments for the 8 k-steps (rows = heads, k = dims).
+  uint32_t qa[8][4];
+  {
+    const uint32_t qbase = smem_u32(q_smem);
+    const int mat = lane >> 3, r8 = lane & 7;
+    const int row = (mat & 1) * 8 + r8;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int c = 2 * kk + (mat >> 1);  // 16-byte chunk index 0..15 in the 256-byte row
+      const uint32_t addr = qbase + row * 256 + ((((c & 7) ^ (row & 7)) | (c & 8)) << 4);
+      ldsm_x4(addr, qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+    }
+  }
+
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const float sl2 = args.scale_log2;
+  const int key_base = warp * 16;
+  bool ok = true;
+
+  for (int i = 0; i < n_pages; ++i) {
+    const int s = i % kStages;
+    ok = mbar_wait(&sm->full[s], (i / kStages) & 1, args.status, abort_flag);
+    if (!ok) break;
+    const uint32_t st = smem_u32(stages + s * kStageBytes);
+    // ---- S = Q K^T for keys key_base .. key_base+15 of this page.
+    float sc[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+    {
+      const int mat = lane >> 3, r8 = lane & 7;
+      const int key = key_base + (mat >> 1) * 8 + r8;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int dim0 = 16 * kk + (mat & 1) * 8;
+        const uint32_t addr = st + (dim0 >> 6) * kBoxBytes + sw128(key, (dim0 & 63) >> 3);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(addr, b0, b1, b2, b3);
+        mma_bf16_16816(sc[0], qa[kk], b0, b1);
+        mma_bf16_16816(sc[1], qa[kk], b2, b3);
+      }
+    }
+    // ---- causal / length mask (only pages that reach past t_lim)
+    const int page_key0 = sm->pages[i] * 64 + key_base;
+    if (page_key0 + 15 > t_lim) {
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = page_key0 + n * 8 + (lane & 3) * 2 + (e & 1);
+          if (key > t_lim) sc[n][e] = -INFINITY;
+        }
+    }
+    // ---- online softmax (log2 domain)
+    float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1])) * sl2;
+    float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3])) * sl2;
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
+    const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
+    const float a0 = ex2(m0 - mu0), a1 = ex2(m1 - mu1);
+    m0 = mn0;
+    m1 = mn1;
+    float p[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      p[n][0] = ex2(fmaf(sc[n][0], sl2, -mu0));
+      p[n][1] = ex2(fmaf(sc[n][1], sl2, -mu0));
+      p[n][2] = ex2(fmaf(sc[n][2], sl2, -mu1));
+      p[n][3] = ex2(fmaf(sc[n][3], sl2, -mu1));
+    }
+    l0 = l0 * a0 + (p[0][0] + p[0][1] + p[1][0] + p[1][1]);
+    l1 = l1 * a1 + (p[0][2] + p[0][3] + p[1][2] + p[1][3]);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= a0;
+      o[j][1] *= a0;
+      o[j][2] *= a1;
+      o[j][3] *= a1;
+    }
+    uint32_t pa[4];
+    pa[0] = pack_bf16x2(p[0][0], p[0][1]);
+    pa[1] = pack_bf16x2(p[0][2], p[0][3]);
+    pa[2] = pack_bf16x2(p[1][0], p[1][1]);
+    pa[3] = pack_bf16x2(p[1][2], p[1][3]);
+    // ---- O += P V for the same 16 keys.
+    {
+      const int mat = lane >> 3, r8 = lane & 7;
+      const int key = key_base + (mat & 1) * 8 + r8;
+      const uint32_t vbase = st + 2 * kBoxBytes;
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) {
+        const int dim0 = 8 * j + (mat >> 1) * 8;
+        const uint32_t addr = vbase + (dim0 >> 6) * kBoxBytes + sw128(key, (dim0 & 63) >> 3);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(addr, b0, b1, b2, b3);
+        mma_bf16_16816(o[j], pa, b0, b1);
+        mma_bf16_16816(o[j + 1], pa, b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm->empty[s]);
+  }
+
+  // ---- merge the four warps' partial softmax states
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const int r0 = lane >> 2, r1 = r0 + 8;
+  if ((lane & 3) == 0) {
+    sm->m_part[warp][r0] = m0;
+    sm->m_part[warp][r1] = m1;
+    sm->l_part[warp][r0] = l0;
+    sm->l_part[warp][r1] = l1;
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  float mt0 = -INFINITY, mt1 = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    mt0 = fmaxf(mt0, sm->m_part[w][r0]);
+    mt1 = fmaxf(mt1, sm->m_part[w][r1]);
+  }
+  const float mu0 = mt0 == -INFINITY ? 0.f : mt0;
+  const float mu1 = mt1 == -INFINITY ? 0.f : mt1;
+  float lt0 = 0.f, lt1 = 0.f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    lt0 += sm->l_part[w][r0] * ex2(sm->m_part[w][r0] - mu0);
+    lt1 += sm->l_part[w][r1] * ex2(sm->m_part[w][r1] - mu1);
+  }
+  const float f0 = (lt0 > 0.f ? ex2(m0 - mu0) / lt0 : 0.f);
+  const float f1 = (lt1 > 0.f ? ex2(m1 - mu1) / lt1 : 0.f);
+  // Stage memory is idle once every page was consumed: sum partial O there.
+  float* acc = reinterpret_cast<float*>(stages);  // [4 warps][16 rows][128 dims]
+  {
+    float* mine = acc + warp * 16 * 128;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int col = 8 * j + (lane & 3) * 2;
+      *reinterpret_cast<float2*>(&mine[r0 * 128 + col]) = make_float2(o[j][0] * f0, o[j][1] * f0);
+      *reinterpret_cast<float2*>(&mine[r1 * 128 + col]) = make_float2(o[j][2] * f1, o[j][3] * f1);
+    }
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  {
+    // 128 threads x 16 outputs: thread -> (row, 16 consecutive dims).
+    const int row = threadIdx.x >> 3;
+    const int col0 = (threadIdx.x & 7) * 16;
+    if (row < HG) {
+      float sum[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) sum[c] = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w)
+#pragma unroll
+        for (int c = 0; c < 16; c += 4) {
+          const float4 x = *reinterpret_cast<const float4*>(&acc[(w * 16 + row) * 128 + col0 + c]);
+          sum[c] += x.x;
+          sum[c + 1] += x.y;
+          sum[c + 2] += x.z;
+          sum[c + 3] += x.w;
+        }
+      uint4 packed[2];
+      uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) pw[c] = pack_bf16x2(sum[2 * c], sum[2 * c + 1]);
+      uint4* dst = reinterpret_cast<uint4*>(args.out + (t * args.num_heads + g * HG + row) * 128 + col0);
+      dst[0] = packed[0];
+      dst[1] = packed[1];
+      if (args.lse != nullptr && (threadIdx.x & 7) == 0) {
+        float mt = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) mt = fmaxf(mt, sm->m_part[w][row]);
+        const float mu = mt == -INFINITY ? 0.f : mt;
+        float lt = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) lt += sm->l_part[w][row] * ex2(sm->m_part[w][row] - mu);
+        args.lse[static_cast<int64_t>(g * HG + row) * args.total_q + t] =
+            lt > 0.f ? (mt + __log2f(lt)) * 0.69314718055994531f : INFINITY;
+      }
+    }
+  }
+  (void)ok;
+}
+
+size_t attn_smem_bytes() { return 1024 + kStages * kStageBytes + 16 * 256 + sizeof(AttnSmem); }
+
+}  // namespace
+
+cudaError_t launch_sparse_attn(const AttnArgs& args, cudaStream_t stream) {
+  const int64_t grid = args.total_q * args.num_groups;
+  if (grid == 0) return cudaSuccess;
+  const size_t smem = attn_smem_bytes();
+  const int hg = args.num_heads / args.num_groups;
+  cudaError_t err;
+  if (hg == 16) {
+    err = cudaFuncSetAttribute(sparse_attn_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+    sparse_attn_kernel<16><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
+  } else if (hg == 8) {
+    err = cudaFuncSetAttribute(sparse_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+    sparse_attn_kernel<8><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace ls

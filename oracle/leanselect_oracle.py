@@ -581,3 +581,40 @@ def synthetic_layer(seq_lens, *, num_heads: int = 32, num_kv_heads: int = 2, hea
     if bf16:
         q, k, v = bf16_round(q), bf16_round(k), bf16_round(v)
     return LayerInputs(q, k, v, cu, params, hot)
+
+
+def select_rows(q: np.ndarray, kc: np.ndarray, params: SelectorParams, rows, *, take: int,
+                init_blocks: int = 1, local_blocks: int = 2, block_size: int = 64,
+                kernel_stride: int = 16, policy: str = "bf16") -> Selection:
+    """The selection of a few rows of ONE sequence (``q [N, H, D]``, ``kc [A, G, D]``).
+
+    Same math as :func:`lightweight_compressed_attention` restricted to
+    ``rows`` (relative positions), so the long BASELINE configurations can be
+    checked on a sample without scoring every row.  ``take`` is the output
+    width (``min(topk, P)`` for a single sequence).
+    """
+    rows = np.asarray(rows, dtype=np.int64)
+    n = q.shape[0]
+    q_fused, kv_fused = fold_weights(params, policy)
+    qs = project_queries(q[rows], q_fused, params.num_kv_heads, policy)
+    ks = project_atom_keys(kc, kv_fused, policy)
+    pages = pool_atoms_to_pages(atom_scores(qs, ks), n, block_size, kernel_stride)
+    g, r, p = pages.shape
+    qpage = rows // block_size
+    page_ids = np.arange(p)
+    visible = page_ids[None, :] <= qpage[:, None]
+    local = visible & (page_ids[None, :] + local_blocks >= qpage[:, None])
+    forced = (page_ids < init_blocks)[None, :] | local
+    masked = np.where(visible[None], pages, NEG_INF).astype(np.float32)
+    masked = np.where((forced & visible)[None], POS_INF, masked).astype(np.float32)
+    k = min(take, p)
+    order = np.argsort(-masked, axis=-1, kind="stable")[..., :k]
+    vals = np.take_along_axis(masked, order, axis=-1)
+    valid = ~(np.isnan(vals) | np.isneginf(vals))
+    chosen = np.where(valid, order, -1)
+    idx = np.full((g, r, take), -1, dtype=np.int32)
+    idx[..., :k] = np.sort(np.where(chosen < 0, np.iinfo(np.int32).max, chosen), axis=-1)
+    idx = np.where(idx == np.iinfo(np.int32).max, -1, idx).astype(np.int32)
+    finite_vals = np.where(valid & np.isfinite(vals), vals, POS_INF)
+    boundary = np.where(valid.any(-1), finite_vals.min(-1), np.nan).astype(np.float32)
+    return Selection(idx, boundary, [(0, masked)])

@@ -1,0 +1,353 @@
+"""CUDA kernels vs the CPU oracle on seeded inputs (needs a B200).
+
+Tolerances:
+* compression and weight folding: bit-exact (same fp32 summation order);
+* projections: within one bf16 ulp, >= 99% bit-exact;
+* page scores: |gpu - oracle| <= 2e-3 + 2e-3*|oracle| (fp32 accumulation order);
+* page selection: identical sets per row except pages whose oracle score is
+  within 1e-3 relative of the row's budget-boundary score;
+* attention output: max abs <= 2e-2, mean abs <= 2e-3 vs the fp32 oracle, and
+  the error RMS below 1% of the output RMS.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import leanselect_oracle as ora
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover - collected on CPU too
+    pytest.skip("needs CUDA", allow_module_level=True)
+
+import leanselect_b200 as lsb  # noqa: E402
+from leanselect_b200 import ops  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+
+
+def to_dev(x, dtype=torch.bfloat16):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(DEV, dtype)
+
+
+def cu_dev(cu):
+    return torch.from_numpy(np.asarray(cu, dtype=np.int32)).to(DEV)
+
+
+def selector_for(params: ora.SelectorParams) -> lsb.LeanSelectSelector:
+    sel = lsb.LeanSelectSelector(num_heads=params.num_heads, num_kv_heads=params.num_kv_heads,
+                                 head_dim=params.head_dim, router_heads=params.q_proj.shape[0],
+                                 router_dim=params.q_proj.shape[2])
+    with torch.no_grad():
+        sel.head_mix.copy_(torch.from_numpy(params.head_mix))
+        sel.kv_head_mix.copy_(torch.from_numpy(params.kv_head_mix))
+        sel.q_proj.copy_(torch.from_numpy(params.q_proj))
+        sel.k_proj.copy_(torch.from_numpy(params.k_proj))
+    return sel.to(DEV)
+
+
+@pytest.fixture(autouse=True)
+def clean_status():
+    torch.cuda.synchronize()
+    ops.status_word(DEV).zero_()
+    yield
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------
+# a2: folding
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("router", [(32, 4), (4, 32)])
+def test_fold_weights_exact(router):
+    rng = np.random.default_rng(3)
+    params = ora.selector_params(32, 2, 128, router[0], router[1], rng)
+    params.kv_head_mix = (1 + 0.1 * rng.standard_normal(params.kv_head_mix.shape)).astype(np.float32)
+    sel = selector_for(params)
+    qf, kf = sel.fused_weights()
+    eq, ek = ora.fold_weights(params, "fp32")
+    np.testing.assert_array_equal(qf.cpu().numpy(), eq)
+    np.testing.assert_array_equal(kf.cpu().numpy(), ek)
+    qb, kb = sel.fused_weights(dtype=torch.bfloat16)
+    eqb, ekb = ora.fold_weights(params, "bf16")
+    np.testing.assert_array_equal(qb.float().cpu().numpy(), eqb)
+    np.testing.assert_array_equal(kb.float().cpu().numpy(), ekb)
+    w = sel.kernel_weights()
+    # Kernel layout: wq_t[g, f, s*D + d] = q_fused[g*Hg + s, d, f].
+    wq = w.wq_t.float().cpu().numpy().reshape(2, 128, 16, 128).transpose(0, 2, 3, 1)
+    np.testing.assert_array_equal(wq.reshape(32, 128, 128), eqb)
+    np.testing.assert_array_equal(w.wk_t.float().cpu().numpy().transpose(0, 2, 1), ekb)
+
+
+# ---------------------------------------------------------------------------
+# a1: compression
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("geometry", [(32, 16), (128, 64), (64, 16)])
+def test_compress_keys_bit_exact(geometry):
+    ks_, st = geometry
+    lens = [1000, 31, 32, 47, 0, 129, 3000, 1]
+    inp = ora.synthetic_layer(lens, num_heads=4, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=2, seed=11, bf16=True)
+    kc, cu_c = ops.compress_keys(to_dev(inp.k), cu_dev(inp.cu_seqlens), kernel_size=ks_,
+                                 kernel_stride=st)
+    ekc, ecu = ora.compress_keys(inp.k, inp.cu_seqlens, kernel_size=ks_, kernel_stride=st,
+                                 policy="bf16")
+    np.testing.assert_array_equal(cu_c.cpu().numpy(), ecu)
+    np.testing.assert_array_equal(kc.float().cpu().numpy(), ekc)
+    assert ops.check_status(DEV) == 0
+
+
+def test_compress_module_matches_reference_contract():
+    inp = ora.synthetic_layer([300, 20], num_heads=4, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=1, seed=5, bf16=True)
+    module = lsb.CompressK(2, 128, kernel_size=32, kernel_stride=16)
+    kc, cu = module(to_dev(inp.k), cu_dev(inp.cu_seqlens))
+    assert kc.shape == (17, 2, 128) and kc.dtype == torch.bfloat16
+    assert cu.tolist() == [0, 17, 17]
+
+
+# ---------------------------------------------------------------------------
+# a3/a4: projections
+# ---------------------------------------------------------------------------
+
+def _ulp_close(actual, expected, frac=0.99):
+    a, e = np.asarray(actual, np.float32), np.asarray(expected, np.float32)
+    np.testing.assert_allclose(a, e, rtol=2 ** -7, atol=1e-6)
+    assert np.mean(a == e) >= frac, np.mean(a == e)
+
+
+@pytest.mark.parametrize("heads", [(32, 2), (16, 2)])
+def test_project_queries(heads):
+    h, g = heads
+    inp = ora.synthetic_layer([1000], num_heads=h, num_kv_heads=g, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=2, seed=21, bf16=True)
+    sel = selector_for(inp.params)
+    qs = sel.project_queries(to_dev(inp.q))
+    qf, _ = ora.fold_weights(inp.params, "bf16")
+    _ulp_close(qs.float().cpu().numpy(), ora.project_queries(inp.q, qf, g, "bf16"))
+
+
+def test_project_atom_keys():
+    inp = ora.synthetic_layer([3000], num_heads=32, num_kv_heads=2, head_dim=128, router_heads=32,
+                              router_dim=4, hot_pages=5, seed=22, bf16=True)
+    sel = selector_for(inp.params)
+    kc, _ = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    ks = sel.project_atom_keys(to_dev(kc))
+    _, kf = ora.fold_weights(inp.params, "bf16")
+    _ulp_close(ks.float().cpu().numpy(), ora.project_atom_keys(kc, kf, "bf16"))
+
+
+# ---------------------------------------------------------------------------
+# a5/a6: page scores
+# ---------------------------------------------------------------------------
+
+def test_score_pages_single_sequence_api():
+    inp = ora.synthetic_layer([1500], num_heads=32, num_kv_heads=2, head_dim=128, router_heads=32,
+                              router_dim=4, hot_pages=5, seed=23, bf16=True)
+    sel = selector_for(inp.params)
+    kc, _ = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    got = sel.score_pages(to_dev(inp.q), to_dev(kc), seq_len=1500, block_size=64,
+                          kernel_stride=16).float().cpu().numpy()
+    want = ora.score_pages(inp.q, kc, inp.params, seq_len=1500, policy="bf16")
+    assert got.shape == want.shape == (2, 1500, 24)
+    np.testing.assert_allclose(got, want, rtol=2e-3, atol=2e-3)
+
+
+def test_score_pages_packed_batch():
+    lens = [700, 64, 65, 20, 1300]
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=3, seed=24, bf16=True)
+    sel = selector_for(inp.params)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    w = sel.kernel_weights()
+    ks = ops.project_atom_keys(to_dev(kc), w.wk_t)
+    got = ops.score_pages(to_dev(inp.q), w, ks, cu_dev(inp.cu_seqlens), cu_dev(cu_c),
+                          max(lens)).cpu().numpy()
+    for b, n in enumerate(lens):
+        q0, c0, c1 = inp.cu_seqlens[b], cu_c[b], cu_c[b + 1]
+        p = (n + 63) // 64
+        if c1 > c0:
+            want = ora.score_pages(inp.q[q0:q0 + n], kc[c0:c1], inp.params, seq_len=n,
+                                   policy="bf16")
+            np.testing.assert_allclose(got[:, q0:q0 + n, :p], want, rtol=2e-3, atol=2e-3)
+        else:
+            assert np.all(np.isneginf(got[:, q0:q0 + n, :p]))
+        assert np.all(np.isneginf(got[:, q0:q0 + n, p:]))
+
+
+# ---------------------------------------------------------------------------
+# a7/a8: selection
+# ---------------------------------------------------------------------------
+
+SELECT_CASES = [
+    # lens, H, G, R, r, topk, init, local
+    ([2000], 32, 2, 32, 4, 35, 1, 2),
+    ([700, 130, 20, 64, 65, 1500], 32, 2, 4, 32, 12, 1, 2),
+    ([900], 32, 2, 4, 32, 100, 1, 2),       # budget wider than most rows' visible pages
+    ([1100, 257], 32, 2, 4, 32, 9, 1, 0),   # no local pages
+    ([1300], 32, 2, 4, 32, 11, 3, 4),       # several sinks
+    ([1000, 2100], 16, 2, 4, 32, 20, 1, 2),  # 8 heads per group
+    ([4096], 32, 2, 4, 32, 128, 1, 2),      # the largest budget
+]
+
+
+def _run_selection(lens, h, g, rh, rd, topk, init, local, seed):
+    inp = ora.synthetic_layer(lens, num_heads=h, num_kv_heads=g, head_dim=128, router_heads=rh,
+                              router_dim=rd, hot_pages=4, seed=seed, bf16=True)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    module = lsb.LayerConfig(topk=topk, init_blocks=init, local_blocks=local)
+    from leanselect_b200.attention import _LayerView
+    view = _LayerView(module, selector_for(inp.params))
+    got = lsb.lightweight_compressed_attention(view, to_dev(inp.q), to_dev(kc),
+                                               cu_dev(inp.cu_seqlens), cu_dev(cu_c), max(lens))
+    return inp, kc, cu_c, got
+
+
+@pytest.mark.parametrize("case", range(len(SELECT_CASES)))
+def test_select_pages_matches_oracle(case):
+    lens, h, g, rh, rd, topk, init, local = SELECT_CASES[case]
+    inp, kc, cu_c, got = _run_selection(lens, h, g, rh, rd, topk, init, local, seed=40 + case)
+    want = ora.lightweight_compressed_attention(inp.q, kc, inp.cu_seqlens, cu_c, inp.params,
+                                                topk=topk, init_blocks=init, local_blocks=local,
+                                                policy="bf16")
+    got_np = got.cpu().numpy()
+    assert got.dtype == torch.int32 and got_np.shape == want.topk_idx.shape
+    bad = ora.selection_mismatches(got_np, want, rel_tol=1e-3)
+    assert not bad, bad[:5]
+    # No duplicates, padding only at the end of each row.
+    for row in got_np.reshape(-1, got_np.shape[-1])[::97]:
+        valid = row[row >= 0]
+        assert len(set(valid.tolist())) == len(valid)
+        assert np.all(row[len(valid):] == -1)
+    assert ops.check_status(DEV) == 0
+
+
+def test_select_config1_rows():
+    """BASELINE config 1 (N=32768, 32/2 heads, T=67, bf16) on a row sample."""
+    n = 32768
+    inp = ora.synthetic_layer([n], seed=1, bf16=True)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    module = lsb.LayerConfig(topk=67)
+    from leanselect_b200.attention import _LayerView
+    view = _LayerView(module, selector_for(inp.params))
+    got = lsb.lightweight_compressed_attention(view, to_dev(inp.q), to_dev(kc),
+                                               cu_dev(inp.cu_seqlens), cu_dev(cu_c), n).cpu().numpy()
+    rng = np.random.default_rng(0)
+    rows = np.unique(np.concatenate([np.arange(0, 130), np.arange(n - 70, n),
+                                     rng.integers(0, n, 200)]))
+    want = ora.select_rows(inp.q, kc, inp.params, rows, take=67)
+    bad = ora.selection_mismatches(got[:, rows], want, rel_tol=1e-3)
+    assert not bad, bad[:5]
+
+
+# ---------------------------------------------------------------------------
+# a9: sparse attention
+# ---------------------------------------------------------------------------
+
+def _attn_check(out, lse, want_out, want_lse, rows=None):
+    o = out.float().cpu().numpy()
+    if rows is not None:
+        o, want_out = o[rows], want_out[rows]
+    err = np.abs(o - want_out)
+    assert err.max() <= 2e-2, err.max()
+    assert err.mean() <= 2e-3, err.mean()
+    rms = np.sqrt(np.mean(want_out ** 2))
+    assert np.sqrt(np.mean(err ** 2)) <= 0.01 * rms + 1e-6
+    if lse is not None:
+        l = lse.cpu().numpy()
+        if rows is not None:
+            l, want_lse = l[:, rows], want_lse[:, rows]
+        fin = np.isfinite(want_lse)
+        assert np.array_equal(fin, np.isfinite(l))
+        np.testing.assert_allclose(l[fin], want_lse[fin], rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("heads", [(32, 2), (16, 2)])
+def test_sparse_attention_with_selected_pages(heads):
+    h, g = heads
+    lens = [900, 130, 20, 1500]
+    inp, kc, cu_c, idx = _run_selection(lens, h, g, 4, 32, 14, 1, 2, seed=60 + h)
+    cu = cu_dev(inp.cu_seqlens)
+    out, lse = ops.sparse_attn(to_dev(inp.q), to_dev(inp.k), to_dev(inp.v), cu, cu, max(lens),
+                               max(lens), idx, return_lse=True)
+    want, want_lse = ora.sparse_attention(inp.q, inp.k, inp.v, inp.cu_seqlens, inp.cu_seqlens,
+                                          idx.cpu().numpy())
+    _attn_check(out, lse, want, want_lse)
+    assert ops.check_status(DEV) == 0
+
+
+def test_sparse_attention_arbitrary_lists():
+    """Unsorted lists with duplicates, -1 holes and future pages; non-causal too."""
+    lens = [700, 333]
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=2, seed=70, bf16=True)
+    total = sum(lens)
+    rng = np.random.default_rng(5)
+    idx = rng.integers(-1, 11, size=(2, total, 9)).astype(np.int32)
+    idx[:, ::3, 4] = idx[:, ::3, 2]                   # duplicates
+    idx[:, 100:110] = -1                              # empty rows
+    idx[:, lens[0]:, :] = np.minimum(idx[:, lens[0]:, :], 5)   # keep sequence 2 in range
+    cu = cu_dev(inp.cu_seqlens)
+    for causal in (True, False):
+        out, lse = ops.sparse_attn(to_dev(inp.q), to_dev(inp.k), to_dev(inp.v), cu, cu,
+                                   max(lens), max(lens), to_dev(idx, torch.int32), causal=causal,
+                                   return_lse=True)
+        want, want_lse = ora.sparse_attention(inp.q, inp.k, inp.v, inp.cu_seqlens, inp.cu_seqlens,
+                                              idx, causal=causal)
+        _attn_check(out, lse, want, want_lse)
+        assert np.all(out[100:110].float().cpu().numpy() == 0)
+    assert ops.check_status(DEV) == 0
+
+
+def test_sparse_attention_flags_out_of_range_pages():
+    lens = [200]
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=1, seed=71, bf16=True)
+    idx = np.zeros((2, 200, 3), dtype=np.int32)
+    idx[:, :, 1] = 50   # past the last page: ignored, flagged
+    idx[:, :, 2] = -1
+    cu = cu_dev(inp.cu_seqlens)
+    out = ops.sparse_attn(to_dev(inp.q), to_dev(inp.k), to_dev(inp.v), cu, cu, 200, 200,
+                          to_dev(idx, torch.int32))
+    want, _ = ora.sparse_attention(inp.q, inp.k, inp.v, inp.cu_seqlens, inp.cu_seqlens, idx)
+    _attn_check(out, None, want, None)
+    with pytest.raises(lsb.LeanSelectError):
+        ops.check_status(DEV)
+
+
+def test_prefill_layer_config1_rows():
+    """Whole hot path at BASELINE config-1 size, checked on sampled rows."""
+    n = 32768
+    inp = ora.synthetic_layer([n], seed=2, bf16=True)
+    sel = selector_for(inp.params)
+    cu = cu_dev(inp.cu_seqlens)
+    out, idx = lsb.prefill_layer_attention(to_dev(inp.q), to_dev(inp.k), to_dev(inp.v), cu, n, sel,
+                                           lsb.LayerConfig(topk=67), return_topk=True)
+    rng = np.random.default_rng(1)
+    rows = np.unique(np.concatenate([np.arange(0, 70), rng.integers(0, n, 120),
+                                     np.arange(n - 40, n)]))
+    want, _ = ora.sparse_attention(inp.q, inp.k, inp.v, inp.cu_seqlens, inp.cu_seqlens,
+                                   idx.cpu().numpy(), rows=rows)
+    _attn_check(out, None, want, None, rows=rows)
+    assert ops.check_status(DEV) == 0
+
+
+# ---------------------------------------------------------------------------
+# Boundary behaviour
+# ---------------------------------------------------------------------------
+
+def test_unsupported_geometry_raises_before_launch():
+    q = torch.zeros(64, 32, 64, dtype=torch.bfloat16, device=DEV)
+    k = torch.zeros(64, 2, 64, dtype=torch.bfloat16, device=DEV)
+    cu = cu_dev([0, 64])
+    idx = torch.zeros(2, 64, 1, dtype=torch.int32, device=DEV)
+    with pytest.raises(lsb.LeanSelectError) as info:
+        ops.sparse_attn(q, k, k, cu, cu, 64, 64, idx)
+    assert info.value.code == 2  # LS_ERR_UNSUPPORTED
+
+
+def test_cpu_tensors_are_rejected():
+    sel = lsb.LeanSelectSelector(num_heads=32, num_kv_heads=2, head_dim=128)
+    with pytest.raises(RuntimeError):
+        sel.project_queries(torch.zeros(4, 32, 128))

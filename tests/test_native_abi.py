@@ -1,0 +1,125 @@
+"""The C ABI library and the host-side API, without a GPU.
+
+Only calls that fail argument validation are made here: validation happens
+on the host before any CUDA call, so these run on a machine without a GPU.
+"""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import leanselect_b200 as lsb
+from leanselect_b200 import _native
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "leanselect_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^(?:const char\*|int)\s+(ls_\w+)\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.load()
+    names = declared_functions()
+    assert len(names) >= 11
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(_native.SIGNATURES) | set(_native.STRING_FUNCS) == set(names)
+
+
+def test_version_and_status_strings():
+    assert "sm_100a" in lsb.version()
+    lib = _native.load()
+    assert lib.ls_status_string(0) == b"LS_OK"
+    assert lib.ls_status_string(2) == b"LS_ERR_UNSUPPORTED"
+    assert lib.ls_status_string(99) == b"LS_ERR_UNKNOWN"
+
+
+def test_null_pointers_are_rejected():
+    lib = _native.load()
+    rc = lib.ls_sparse_attn(None, None, None, None, None, 1, 1, 1, 1, 1, 32, 2, 128, None, 1, 64,
+                            0.0, 1, None, None, None, None)
+    assert rc == _native.LS_ERR_INVALID_ARGUMENT
+    assert b"null" in lib.ls_last_error()
+
+
+def test_unsupported_geometry_is_reported():
+    lib = _native.load()
+    fake = ctypes.c_void_p(1 << 20)  # never dereferenced: validation fails first
+    rc = lib.ls_select_pages(fake, fake, fake, fake, fake, 1, 64, 64, 3, 32, 2, 64, 128, 5, 1, 2,
+                             64, 16, fake, None, None)
+    assert rc == _native.LS_ERR_UNSUPPORTED
+    rc = lib.ls_select_pages(fake, fake, fake, fake, fake, 1, 64, 64, 3, 32, 2, 128, 128, 129, 1,
+                             2, 64, 16, fake, None, None)
+    assert rc == _native.LS_ERR_UNSUPPORTED  # take > LS_MAX_TOPK
+    rc = lib.ls_sparse_attn(fake, fake, fake, fake, fake, 1, 64, 64, 64, 64, 24, 2, 128, fake, 4,
+                            64, 0.0, 1, fake, None, None, None)
+    assert rc == _native.LS_ERR_UNSUPPORTED  # 12 heads per group
+    rc = lib.ls_compress_keys(fake, fake, 1, 64, 2, 128, 48, 16, fake, fake, 3, None, None)
+    assert rc == _native.LS_ERR_UNSUPPORTED  # kernel_size/stride = 3
+
+
+def test_misaligned_pointer_is_reported():
+    lib = _native.load()
+    fake = ctypes.c_void_p(1 << 20)
+    odd = ctypes.c_void_p((1 << 20) + 2)
+    rc = lib.ls_sparse_attn(odd, fake, fake, fake, fake, 1, 64, 64, 64, 64, 32, 2, 128, fake, 4,
+                            64, 0.0, 1, fake, None, None, None)
+    assert rc == _native.LS_ERR_ALIGNMENT
+
+
+def test_selector_geometry_errors_match_reference():
+    """Constructor checks of selector.py:81-94."""
+    for kwargs in ({"num_heads": 7}, {"router_heads": 9}, {"head_dim": 0}):
+        config = dict(num_heads=8, num_kv_heads=2, head_dim=8)
+        config.update(kwargs)
+        with pytest.raises(ValueError):
+            lsb.LeanSelectSelector(**config)
+
+
+def test_selector_shape_errors_match_reference():
+    """project_* reject bad shapes with ValueError (selector.py:161-166, 180-186)."""
+    sel = lsb.LeanSelectSelector(num_heads=8, num_kv_heads=2, head_dim=8, router_heads=2,
+                                 router_dim=4)
+    with pytest.raises(ValueError):
+        sel.project_queries(torch.randn(2, 3, 8))
+    with pytest.raises(ValueError):
+        sel.project_atom_keys(torch.randn(2, 3, 8))
+
+
+def test_product_path_has_no_cpu_fallback():
+    sel = lsb.LeanSelectSelector(num_heads=32, num_kv_heads=2, head_dim=128)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sel.project_queries(torch.zeros(4, 32, 128))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        lsb.ops.sparse_attn(torch.zeros(4, 32, 128), torch.zeros(4, 2, 128),
+                            torch.zeros(4, 2, 128), torch.tensor([0, 4]), torch.tensor([0, 4]),
+                            4, 4, torch.zeros(2, 4, 1, dtype=torch.int32))
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    with pytest.raises(RuntimeError, match="not found"):
+        _native.load(tmp_path / "missing.so")
+
+
+def test_selector_initialisation_matches_reference_rule():
+    """reset_parameters (selector.py:112-137): group mean mix, scaled orthonormal frame."""
+    torch.manual_seed(7)
+    sel = lsb.LeanSelectSelector(num_heads=8, num_kv_heads=2, head_dim=8, router_heads=2,
+                                 router_dim=4)
+    assert torch.allclose(sel.head_mix, torch.full((8, 2), 0.25))
+    assert torch.all(sel.kv_head_mix == 1)
+    frame = sel.q_proj.permute(1, 0, 2).reshape(8, 8) * 8 ** 0.25
+    assert torch.allclose(frame.T @ frame, torch.eye(8), atol=1e-5)
+    assert torch.equal(sel.q_proj, sel.k_proj)
+
+
+def test_reference_budget_mapping():
+    """Budget arithmetic of load_model / the attention module (minicpm.py:1965-1966)."""
+    cfg = lsb.LayerConfig()
+    assert (cfg.topk, cfg.local_blocks, cfg.init_blocks) == (67, 2, 1)
+    assert lsb.ops.atom_count(31) == 0 and lsb.ops.atom_count(32768) == 2047
