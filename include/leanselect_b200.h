@@ -163,6 +163,21 @@ int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
                     int32_t kernel_stride, int32_t* topk_idx, int32_t* status, void* stream);
 
 /*
+ * ls_select_pages_chunk -- ls_select_pages for a slice of ONE sequence, used
+ * by the sequence-parallel prefill (no reference counterpart: the reference
+ * prefill runs on one GPU).  q holds chunk_q query rows at positions
+ * [q_position, q_position + chunk_q) of a sequence of seq_len tokens whose
+ * total_c atoms are all of ks [G, total_c, F].  Visibility, forced pages and
+ * the output width `take` follow ls_select_pages with P = ceil(seq_len/64).
+ */
+int ls_select_pages_chunk(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                          int64_t chunk_q, int32_t q_position, int32_t seq_len, int64_t total_c,
+                          int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t width,
+                          int32_t take, int32_t init_blocks, int32_t local_blocks,
+                          int32_t block_size, int32_t kernel_stride, int32_t* topk_idx,
+                          int32_t* status, void* stream);
+
+/*
  * ls_sparse_attn -- replaces infllmv2_attn_varlen_func(..., topk_idx=)
  * (called at leanselect/models/minicpm.py:3229-3243; InfLLM-v2 varlen_fwd
  * with a block mask, third_party/infllmv2/paper1.patch).

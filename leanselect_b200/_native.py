@@ -40,6 +40,8 @@ SIGNATURES = {
                        _I32, _P, _P, _P],
     "ls_select_pages": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _I32,
                         _I32, _I32, _I32, _I32, _P, _P, _P],
+    "ls_select_pages_chunk": [_P, _P, _P, _I64, _I32, _I32, _I64, _I32, _I32, _I32, _I32, _I32,
+                              _I32, _I32, _I32, _I32, _P, _P, _P],
     "ls_sparse_attn": [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _P,
                        _I32, _I32, _F32, _I32, _P, _P, _P, _P],
 }

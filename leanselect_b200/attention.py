@@ -152,22 +152,57 @@ class _LayerView:
         self.num_key_value_heads = selector.num_kv_heads
 
 
+def count_attended_keys(topk_idx: torch.Tensor, lengths, block_size: int = 64,
+                        positions: torch.Tensor | None = None) -> int:
+    """Number of (group, token, key) triples the sparse attention computes.
+
+    Counts, for each token, the keys of its selected pages that are causally
+    visible (each page at most once; the selection never repeats a page).
+    Used to state the attention's algorithmic FLOPs (4 * D * Hg per triple).
+    ``positions`` (token positions inside their sequences) replaces
+    ``lengths`` for query chunks of a longer sequence.
+    """
+    dev = topk_idx.device
+    if positions is None:
+        pos = torch.cat([torch.arange(int(n), device=dev) for n in lengths])
+    else:
+        pos = positions.to(dev)
+    start = topk_idx.long() * block_size
+    visible = torch.clamp(torch.minimum(start + block_size, pos[None, :, None] + 1) - start, min=0)
+    return int((visible * (topk_idx >= 0)).sum().item())
+
+
 def prefill_layer_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                             cu_seqlens: torch.Tensor, max_seqlen: int,
                             selector: LeanSelectSelector, cfg: LayerConfig, *, lengths=None,
-                            return_topk: bool = False):
+                            return_topk: bool = False, timers: list | None = None):
     """Compress -> select -> sparse attention for one layer's packed prefill.
 
     ``q [total, H, D]``, ``k``/``v [total, G, D]`` are post-RoPE; queries and
     keys share ``cu_seqlens`` (prefill).  Returns ``out [total, H, D]`` (and
-    ``topk_idx`` with ``return_topk``).
+    ``topk_idx`` with ``return_topk``).  ``timers`` (optional list) receives
+    ``(stage, start_event, end_event)`` for the stages ``compress``,
+    ``select`` and ``attn`` on the current stream.
     """
+    def mark():
+        if timers is None:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return ev
+
     lens = list(lengths) if lengths is not None else ops.host_lengths(cu_seqlens)
+    e0 = mark()
     kc, cu_c = ops.compress_keys(k, cu_seqlens, kernel_size=cfg.kernel_size,
                                  kernel_stride=cfg.kernel_stride, lengths=lens)
+    e1 = mark()
     view = _LayerView(cfg, selector)
     idx = lightweight_compressed_attention(view, q, kc, cu_seqlens, cu_c, max_seqlen,
                                            q_lengths=lens)
+    e2 = mark()
     out = ops.sparse_attn(q, k, v, cu_seqlens, cu_seqlens, max_seqlen, max_seqlen, idx,
                           causal=True)
+    e3 = mark()
+    if timers is not None:
+        timers.extend([("compress", e0, e1), ("select", e1, e2), ("attn", e2, e3)])
     return (out, idx) if return_topk else out

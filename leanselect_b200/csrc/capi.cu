@@ -305,6 +305,45 @@ int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
   return err == cudaSuccess ? LS_OK : cuda_fail(err, "select_pages launch");
 }
 
+int ls_select_pages_chunk(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                          int64_t chunk_q, int32_t q_position, int32_t seq_len, int64_t total_c,
+                          int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t width,
+                          int32_t take, int32_t init_blocks, int32_t local_blocks,
+                          int32_t block_size, int32_t kernel_stride, int32_t* topk_idx,
+                          int32_t* status, void* stream) {
+  int rc = check_score_common(q, wq_t, chunk_q, num_heads, num_kv_heads, head_dim, width);
+  if (rc != LS_OK) return rc;
+  LS_REQUIRE(q_position >= 0 && seq_len >= 0 && total_c >= 0, "bad sizes");
+  LS_REQUIRE(q_position + chunk_q <= seq_len, "query chunk extends past the sequence");
+  LS_REQUIRE(take >= 0 && init_blocks >= 0 && local_blocks >= 0, "negative budget");
+  if (block_size != 64 || kernel_stride != 16)
+    return fail(LS_ERR_UNSUPPORTED, "block_size must be 64 and kernel_stride 16");
+  if (take > LS_MAX_TOPK) return fail(LS_ERR_UNSUPPORTED, "take exceeds LS_MAX_TOPK");
+  if (seq_len > 65536 * 64)
+    return fail(LS_ERR_UNSUPPORTED, "sequences longer than 4M tokens are not supported");
+  if (chunk_q == 0 || take == 0) return LS_OK;
+  LS_REQUIRE(topk_idx, "null topk_idx");
+  LS_REQUIRE(total_c == 0 || ks, "null ks");
+  if (ks) LS_REQUIRE_ALIGNED(ks);
+  ScoreArgs a{};
+  rc = build_score_args(&a, q, wq_t, ks, chunk_q, total_c, num_heads, num_kv_heads);
+  if (rc != LS_OK) return rc;
+  a.cu_q = nullptr;
+  a.cu_c = nullptr;
+  a.batch = 1;
+  a.max_seqlen_q = static_cast<int>(chunk_q);
+  a.take = take;
+  a.init_blocks = init_blocks;
+  a.local_blocks = local_blocks;
+  a.max_pages = (seq_len + 63) / 64;
+  a.pos_offset = q_position;
+  a.seq_len = seq_len;
+  a.topk_idx = topk_idx;
+  a.status = status;
+  const cudaError_t err = launch_score(kModeSelect, a, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? LS_OK : cuda_fail(err, "select_pages_chunk launch");
+}
+
 int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                    const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t batch,
                    int32_t max_seqlen_q, int32_t max_seqlen_k, int64_t total_q, int64_t total_k,

@@ -44,6 +44,8 @@ struct ScoreArgs {
   int init_blocks;
   int local_blocks;
   int max_pages;       // ceil(max_seqlen_q / 64): width of page_scores
+  int pos_offset;      // chunk mode: position of query row 0 inside its sequence
+  int seq_len;         // chunk mode: length of the whole sequence (0 = rows are the sequence)
   int32_t* topk_idx;   // kModeSelect
   float* page_scores;  // kModeScore
   uint16_t* qs_out;    // kModeProject: [G, total_q, F] bf16

@@ -111,98 +111,57 @@ __global__ void compressed_seqlens_kernel(const int32_t* __restrict__ cu_k, int 
 // Key compression (CompressK.forward, minicpm.py:1169-1185)
 // ---------------------------------------------------------------------------
 //
-// One thread owns one 16-byte vector (8 channels) of the [G*D] row and a chunk
-// of kChunk consecutive packed atoms.  It streams the keys once: run sums of
-// `stride` tokens are kept in registers and atom i is the ordered sum of runs
-// i .. i+R-1 (R = kernel_size / stride), times 1/kernel_size, rounded to bf16.
-// The order of the fp32 additions is the oracle's, so results match it
-// bit for bit.  A warp covers one 512-byte key row for G*D = 256.
+// One thread per (packed atom, 16-byte vector of 8 channels).  Consecutive
+// threads cover one key row (512 bytes for G*D = 256), so every load is a
+// fully coalesced row.  A thread sums its window as R = kernel_size / stride
+// runs of `stride` tokens (each run sequentially in fp32), adds the run sums
+// in order, scales by 1/kernel_size and rounds to bf16 -- the oracle's order,
+// so results match it bit for bit.  Each key is read by R atoms; the second
+// read of a run hits L2.
 
-constexpr int kCompressChunk = 8;
-
-template <int R>
-__global__ void compress_keys_kernel(const uint4* __restrict__ k, const int32_t* __restrict__ cu_k,
-                                     const int32_t* __restrict__ cu_c, int batch, int64_t total_k,
-                                     int64_t total_c, int vecs_per_row, int stride,
-                                     float inv_kernel, uint4* __restrict__ kc, int32_t* status) {
-  const int chunks_per_block = blockDim.x / vecs_per_row;
-  const int local_chunk = threadIdx.x / vecs_per_row;
-  const int vec = threadIdx.x % vecs_per_row;
-  if (local_chunk >= chunks_per_block) return;
-  const int64_t chunk = static_cast<int64_t>(blockIdx.x) * chunks_per_block + local_chunk;
-  int64_t atom = chunk * kCompressChunk;
+__global__ void __launch_bounds__(256) compress_keys_kernel(
+    const uint4* __restrict__ k, const int32_t* __restrict__ cu_k, const int32_t* __restrict__ cu_c,
+    int batch, int64_t total_k, int64_t total_c, int vecs_per_row, int runs, int stride,
+    float inv_kernel, uint4* __restrict__ kc, int32_t* status) {
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t atom = gid / vecs_per_row;
+  const int vec = static_cast<int>(gid % vecs_per_row);
   if (atom >= total_c) return;
-  const int64_t atom_end = min(atom + kCompressChunk, total_c);
-
-  int b = find_sequence(cu_c, batch, atom);
-  while (atom < atom_end) {
-    // Skip sequences without atoms (cu_c[b] == cu_c[b+1]).
-    while (b < batch - 1 && static_cast<int64_t>(__ldg(cu_c + b + 1)) <= atom) ++b;
-    const int64_t seq_atom_end = ::min(atom_end, static_cast<int64_t>(__ldg(cu_c + b + 1)));
-    const int64_t local = atom - __ldg(cu_c + b);
-    const int64_t tok0 = __ldg(cu_k + b) + local * stride;
-    if (tok0 + (seq_atom_end - atom - 1 + R) * stride > total_k) {
-      report(status, LS_DEVERR_SEQLENS);
-      return;
-    }
-    float run[R][8];
-    // Runs local .. local+R-2 precede the first atom's last run.
-#pragma unroll
-    for (int j = 0; j < R - 1; ++j) {
-#pragma unroll
-      for (int c = 0; c < 8; ++c) run[j + 1][c] = 0.f;
-      const uint4* src = k + (tok0 + static_cast<int64_t>(j) * stride) * vecs_per_row + vec;
-      for (int t = 0; t < stride; ++t) {
-        const uint4 u = __ldg(src + static_cast<int64_t>(t) * vecs_per_row);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float2 f = __bfloat1622float2(h[c]);
-          run[j + 1][2 * c] += f.x;
-          run[j + 1][2 * c + 1] += f.y;
-        }
-      }
-    }
-    for (int64_t a = atom; a < seq_atom_end; ++a) {
-      // Shift the window: runs[0..R-2] <- runs[1..R-1], then load run R-1.
-#pragma unroll
-      for (int j = 0; j < R - 1; ++j)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) run[j][c] = run[j + 1][c];
-      float nr[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) nr[c] = 0.f;
-      const int64_t t0 = tok0 + (a - atom + R - 1) * stride;
-      const uint4* src = k + t0 * vecs_per_row + vec;
-      for (int t = 0; t < stride; ++t) {
-        const uint4 u = __ldg(src + static_cast<int64_t>(t) * vecs_per_row);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float2 f = __bfloat1622float2(h[c]);
-          nr[2 * c] += f.x;
-          nr[2 * c + 1] += f.y;
-        }
-      }
-#pragma unroll
-      for (int c = 0; c < 8; ++c) run[R - 1][c] = nr[c];
-      float acc[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        acc[c] = 0.f;
-#pragma unroll
-        for (int j = 0; j < R; ++j) acc[c] += run[j][c];
-        acc[c] *= inv_kernel;
-      }
-      uint4 out;
-      out.x = pack_bf16x2(acc[0], acc[1]);
-      out.y = pack_bf16x2(acc[2], acc[3]);
-      out.z = pack_bf16x2(acc[4], acc[5]);
-      out.w = pack_bf16x2(acc[6], acc[7]);
-      kc[a * vecs_per_row + vec] = out;
-    }
-    atom = seq_atom_end;
+  const int b = find_sequence(cu_c, batch, atom);
+  const int64_t local = atom - __ldg(cu_c + b);
+  const int64_t tok0 = __ldg(cu_k + b) + local * stride;
+  if (tok0 + static_cast<int64_t>(runs) * stride > total_k) {
+    report(status, LS_DEVERR_SEQLENS);
+    return;
   }
+  const uint4* src = k + tok0 * vecs_per_row + vec;
+  float acc[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+  for (int j = 0; j < runs; ++j) {
+    float run[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) run[c] = 0.f;
+#pragma unroll 4
+    for (int t = 0; t < stride; ++t) {
+      const uint4 u = __ldg(src + (static_cast<int64_t>(j) * stride + t) * vecs_per_row);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float2 f = __bfloat1622float2(h[c]);
+        run[2 * c] += f.x;
+        run[2 * c + 1] += f.y;
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] += run[c];
+  }
+  uint4 out;
+  out.x = pack_bf16x2(acc[0] * inv_kernel, acc[1] * inv_kernel);
+  out.y = pack_bf16x2(acc[2] * inv_kernel, acc[3] * inv_kernel);
+  out.z = pack_bf16x2(acc[4] * inv_kernel, acc[5] * inv_kernel);
+  out.w = pack_bf16x2(acc[6] * inv_kernel, acc[7] * inv_kernel);
+  kc[atom * vecs_per_row + vec] = out;
 }
 
 // ---------------------------------------------------------------------------
@@ -299,30 +258,12 @@ cudaError_t launch_compress_keys(const uint16_t* k, const int32_t* cu_k, const i
                                  int32_t* status, cudaStream_t stream) {
   if (total_c == 0) return cudaSuccess;
   const int vecs = G * D / 8;
-  const int chunks_per_block = vecs >= 256 ? 1 : 256 / vecs;
-  const int threads = vecs >= 256 ? vecs : chunks_per_block * vecs;
-  const int64_t chunks = (total_c + kCompressChunk - 1) / kCompressChunk;
-  const int64_t blocks = (chunks + chunks_per_block - 1) / chunks_per_block;
-  const float inv = 1.0f / static_cast<float>(kernel_size);
-  const int R = kernel_size / kernel_stride;
-  const uint4* kv = reinterpret_cast<const uint4*>(k);
-  uint4* out = reinterpret_cast<uint4*>(kc);
-  switch (R) {
-    case 1:
-      compress_keys_kernel<1><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-          kv, cu_k, cu_c, batch, total_k, total_c, vecs, kernel_stride, inv, out, status);
-      break;
-    case 2:
-      compress_keys_kernel<2><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-          kv, cu_k, cu_c, batch, total_k, total_c, vecs, kernel_stride, inv, out, status);
-      break;
-    case 4:
-      compress_keys_kernel<4><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-          kv, cu_k, cu_c, batch, total_k, total_c, vecs, kernel_stride, inv, out, status);
-      break;
-    default:
-      return cudaErrorInvalidValue;
-  }
+  const int64_t threads = total_c * vecs;
+  const int64_t blocks = (threads + 255) / 256;
+  compress_keys_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      reinterpret_cast<const uint4*>(k), cu_k, cu_c, batch, total_k, total_c, vecs,
+      kernel_size / kernel_stride, kernel_stride, 1.0f / static_cast<float>(kernel_size),
+      reinterpret_cast<uint4*>(kc), status);
   return cudaGetLastError();
 }
 

@@ -65,6 +65,7 @@ struct TileInfo {
   int64_t c0;       // first packed atom of the sequence
   int atoms;        // atoms of the sequence
   int pages;        // pages of the sequence
+  int pos0;         // position of row 0 inside the sequence (chunk mode), else 0
   int atom_tiles;   // atom tiles the tile needs
   bool prologue;    // whether Qs is computed at all
 };
@@ -88,16 +89,21 @@ __global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constan
     ti.row0 = ti.tile * kRows;
     if (ti.row0 >= ti.n) return;  // whole CTA exits before touching barriers or TMEM
     ti.rows = min(kRows, ti.n - ti.row0);
+    // Null cu_seqlens_c: one sequence whose atoms are all total_c rows of Ks.
     ti.c0 = args.cu_c ? __ldg(args.cu_c + ti.b) : 0;
-    ti.atoms = args.cu_c ? static_cast<int>(__ldg(args.cu_c + ti.b + 1) - ti.c0) : 0;
-    ti.pages = (ti.n + 63) / 64;
+    ti.atoms = args.cu_c ? static_cast<int>(__ldg(args.cu_c + ti.b + 1) - ti.c0)
+                         : static_cast<int>(args.total_c);
+    // Chunk mode: the rows are a slice [pos_offset, pos_offset + n) of a
+    // sequence of seq_len tokens (sequence-parallel prefill).
+    ti.pos0 = args.pos_offset;
+    ti.pages = ((args.seq_len > 0 ? args.seq_len : ti.n) + 63) / 64;
     int needed_atoms = 0;
     if (MODE == kModeScore) {
       needed_atoms = ti.atoms;
     } else if (MODE == kModeSelect) {
       // Candidates of the last row are pages p <= qp_max - local - 1, whose
       // windows end at atom 4p + 3 < 4 (qp_max - local).
-      const int qp_max = (ti.row0 + ti.rows - 1) / 64;
+      const int qp_max = (ti.pos0 + ti.row0 + ti.rows - 1) / 64;
       needed_atoms = max(0, min(ti.atoms, 4 * (qp_max - args.local_blocks)));
     }
     ti.atom_tiles = (needed_atoms + kRows - 1) / kRows;
@@ -238,8 +244,8 @@ __global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constan
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const bool valid = row < ti.rows;
-    const int t_rel = ti.row0 + row;                 // row index inside the sequence
-    const int64_t q_row = ti.q0 + t_rel;             // packed row
+    const int t_rel = ti.pos0 + ti.row0 + row;       // position inside the sequence
+    const int64_t q_row = ti.q0 + ti.row0 + row;     // packed row
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     bool ok = true;
 

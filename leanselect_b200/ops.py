@@ -278,6 +278,33 @@ def select_pages(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
     return idx
 
 
+def select_pages_chunk(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor, *,
+                       q_position: int, seq_len: int, take: int, init_blocks: int = 1,
+                       local_blocks: int = 2, block_size: int = 64,
+                       kernel_stride: int = 16) -> torch.Tensor:
+    """Selection for query rows at ``[q_position, q_position + len(q))`` of one sequence.
+
+    ``ks [G, A, F]`` holds the atoms of the whole sequence (sequence-parallel
+    prefill: each rank selects for its own query chunks).
+    """
+    dev = _require_cuda(q, ks)
+    qb = _bf16(q)
+    n = qb.shape[0]
+    G = weights.num_kv_heads
+    total_c = ks.shape[1]
+    if take > LS_MAX_TOPK:
+        raise ValueError(f"take={take} exceeds LS_MAX_TOPK={LS_MAX_TOPK}")
+    idx = torch.empty(G, n, take, dtype=torch.int32, device=dev)
+    if take == 0 or n == 0:
+        return idx
+    _native.call("ls_select_pages_chunk", qb.data_ptr(), weights.wq_t.data_ptr(),
+                 _ptr(ks) if total_c else None, n, int(q_position), int(seq_len), total_c,
+                 weights.num_heads, G, weights.head_dim, weights.width, int(take),
+                 int(init_blocks), int(local_blocks), block_size, kernel_stride, idx.data_ptr(),
+                 status_word(dev).data_ptr(), _stream(dev))
+    return idx
+
+
 # ---------------------------------------------------------------------------
 # a9: sparse attention
 # ---------------------------------------------------------------------------

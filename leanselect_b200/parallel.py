@@ -1,0 +1,162 @@
+"""Sequence-parallel prefill of one long sequence across the GPUs of a box.
+
+Partition (causal-balanced zig-zag): the sequence is cut into ``2W`` equal
+page-aligned chunks; rank ``r`` owns chunks ``r`` and ``2W-1-r``, so every
+rank holds one early and one late chunk.  Embedding, QKV, RoPE (at the true
+positions), the output projection and the MLP are token-local.  Per layer the
+post-RoPE K and V of all ranks are all-gathered over NCCL into the full
+sequence; each rank compresses the full K (cheap), then selects pages and runs
+the sparse attention for its own two query chunks only
+(``ls_select_pages_chunk`` with the chunk's position offset; ``ls_sparse_attn``
+over the causal key prefix of the chunk).  The last token lives in chunk
+``2W-1``, i.e. on rank 0, which computes the logits.
+
+The partition and gather/reorder helpers are plain host logic over
+``torch.distributed`` and work on any backend (tested with ``gloo`` on CPU).
+"""
+from __future__ import annotations
+
+from typing import Sequence
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .attention import _LayerView, count_attended_keys, lightweight_compressed_attention  # noqa: F401
+from .model import MiniCPMShape, PrefillModel
+
+
+def zigzag_chunks(seq_len: int, world: int, rank: int, align: int = 64):
+    """``[(start, length), (start, length)]`` of the two chunks rank ``rank`` owns."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad world/rank")
+    if seq_len % (2 * world * align):
+        raise ValueError(f"seq_len={seq_len} must be a multiple of 2*world*{align}")
+    c = seq_len // (2 * world)
+    return [(rank * c, c), ((2 * world - 1 - rank) * c, c)]
+
+
+def local_positions(seq_len: int, world: int, rank: int, device=None) -> torch.Tensor:
+    parts = [torch.arange(s, s + n, device=device) for s, n in zigzag_chunks(seq_len, world, rank)]
+    return torch.cat(parts)
+
+
+def gather_sequence(local: torch.Tensor, seq_len: int, group=None) -> torch.Tensor:
+    """All-gather every rank's ``[2C, ...]`` rows and return them in sequence order.
+
+    Rank ``r`` contributes chunks ``r`` and ``2W-1-r`` (in that order).  The
+    result is ``[seq_len, ...]`` with chunk ``c`` at rows ``[cC, (c+1)C)``.
+    """
+    world = dist.get_world_size(group)
+    c = seq_len // (2 * world)
+    if local.shape[0] != 2 * c:
+        raise ValueError("local rows must be two chunks of seq_len / (2 * world)")
+    local = local.contiguous()
+    flat = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                       device=local.device)
+    dist.all_gather_into_tensor(flat, local, group=group)
+    gathered = flat.view((world,) + tuple(local.shape))
+    first = gathered[:, :c]                     # chunk r of rank r      -> chunks 0 .. W-1
+    second = gathered[:, c:].flip(0)            # chunk 2W-1-r of rank r -> chunks W .. 2W-1
+    return torch.cat((first.reshape((-1,) + tuple(local.shape[1:])),
+                      second.reshape((-1,) + tuple(local.shape[1:]))), dim=0)
+
+
+class SequenceParallelRunner:
+    """One sequence prefilled by all ranks of the default process group."""
+
+    def __init__(self, shape: MiniCPMShape, device: torch.device | str, seed: int = 0,
+                 group=None):
+        self.device = torch.device(device)
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        # Same seed on every rank: identical random weights everywhere.
+        self.model = PrefillModel(shape, self.device, seed=seed)
+        self._cu_cache: dict[tuple, torch.Tensor] = {}
+
+    def _cu(self, *values: int) -> torch.Tensor:
+        key = tuple(values)
+        t = self._cu_cache.get(key)
+        if t is None:
+            t = torch.tensor(values, dtype=torch.int32, device=self.device)
+            self._cu_cache[key] = t
+        return t
+
+    def prefill_device(self, ids: torch.Tensor, lengths: Sequence[int], timers: list | None = None,
+                       key_counts: list | None = None):
+        """``ids`` holds the whole sequence on every rank; rank 0 returns ``[1, vocab]`` logits."""
+        if len(lengths) != 1:
+            raise ValueError("sequence-parallel prefill takes one sequence")
+        m, s = self.model, self.model.shape
+        n = int(lengths[0])
+        chunks = zigzag_chunks(n, self.world, self.rank)
+        c = chunks[0][1]
+        local_ids = torch.cat([ids[a:a + c] for a, _ in chunks])
+        positions = local_positions(n, self.world, self.rank, device=self.device)
+        cos, sin = m.rope.tables(positions, n)
+        h = m.embed[local_ids] * s.scale_emb
+        cu_full = self._cu(0, n)
+        cfg = s.sparse
+        pages = (n + cfg.block_size - 1) // cfg.block_size
+        take = min(cfg.topk, pages)
+
+        def mark():
+            if timers is None:
+                return None
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            return ev
+
+        for layer in m.layers:
+            q, k, v = m.qkv(layer, h, cos, sin)
+            kv = torch.stack((k.reshape(2 * c, -1), v.reshape(2 * c, -1)), dim=1)
+            full = gather_sequence(kv, n, self.group)           # [n, 2, G*D]
+            k_full = full[:, 0].reshape(n, s.num_kv_heads, s.head_dim).contiguous()
+            v_full = full[:, 1].reshape(n, s.num_kv_heads, s.head_dim).contiguous()
+            del kv, full, k, v
+            e0 = mark()
+            kc, _ = ops.compress_keys(k_full, cu_full, kernel_size=cfg.kernel_size,
+                                      kernel_stride=cfg.kernel_stride, lengths=[n])
+            e1 = mark()
+            weights = layer.selector.kernel_weights()
+            ks = ops.project_atom_keys(kc, weights.wk_t)
+            idxs = []
+            for i, (start, length) in enumerate(chunks):
+                idxs.append(ops.select_pages_chunk(
+                    q[i * c:(i + 1) * c], weights, ks, q_position=start, seq_len=n, take=take,
+                    init_blocks=cfg.init_blocks, local_blocks=cfg.local_blocks,
+                    block_size=cfg.block_size, kernel_stride=cfg.kernel_stride))
+            e2 = mark()
+            attn = torch.empty_like(q)
+            for i, (start, length) in enumerate(chunks):
+                ops.sparse_attn(q[i * c:(i + 1) * c], k_full, v_full, self._cu(0, length),
+                                self._cu(0, start + length), length, start + length, idxs[i],
+                                causal=True, out=attn[i * c:(i + 1) * c])
+            e3 = mark()
+            if timers is not None:
+                timers.extend([("compress", e0, e1), ("select", e1, e2), ("attn", e2, e3)])
+            if key_counts is not None:
+                total = 0
+                for i, (start, length) in enumerate(chunks):
+                    total += count_attended_keys(idxs[i], None, cfg.block_size,
+                                                 positions=positions[i * c:(i + 1) * c])
+                key_counts.append(total)
+            del q, k_full, v_full, kc, ks, idxs
+            h.add_(attn.view(h.shape[0], -1) @ layer.w_o.t(), alpha=m.residual_scale)
+            del attn
+            m.mlp_residual(layer, h)
+        if self.rank == 0:
+            return m.logits(h[-1:])
+        return None
+
+    def __call__(self, ids_host: torch.Tensor, lengths: Sequence[int]):
+        ids = ids_host.to(self.device, non_blocking=True)
+        logits = self.prefill_device(ids, lengths)
+        if logits is None:
+            torch.cuda.current_stream(self.device).synchronize()
+            return None
+        out = torch.empty(logits.shape, dtype=logits.dtype, pin_memory=True)
+        out.copy_(logits, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out

@@ -58,9 +58,13 @@ def bf16_round(x: np.ndarray) -> np.ndarray:
     NaN and infinities pass through unchanged.
     """
     a = np.ascontiguousarray(x, dtype=np.float32)
-    bits = a.view(np.uint32).astype(np.uint64)
-    rounded = (bits + 0x7FFF + ((bits >> 16) & 1)) & 0xFFFF0000
-    out = rounded.astype(np.uint32).view(np.float32).reshape(a.shape)
+    bits = a.view(np.uint32)
+    # uint32 wrap-around only affects NaN encodings, which are restored below.
+    rounded = (bits >> 16) & np.uint32(1)
+    rounded += np.uint32(0x7FFF)
+    rounded += bits
+    rounded &= np.uint32(0xFFFF0000)
+    out = rounded.view(np.float32).reshape(a.shape)
     special = ~np.isfinite(a)
     if special.any():
         out = np.where(special, a, out)
@@ -583,24 +587,25 @@ def synthetic_layer(seq_lens, *, num_heads: int = 32, num_kv_heads: int = 2, hea
     return LayerInputs(q, k, v, cu, params, hot)
 
 
-def select_rows(q: np.ndarray, kc: np.ndarray, params: SelectorParams, rows, *, take: int,
-                init_blocks: int = 1, local_blocks: int = 2, block_size: int = 64,
-                kernel_stride: int = 16, policy: str = "bf16") -> Selection:
-    """The selection of a few rows of ONE sequence (``q [N, H, D]``, ``kc [A, G, D]``).
+def select_for_queries(q_rows: np.ndarray, positions, seq_len: int, kc: np.ndarray,
+                       params: SelectorParams, *, take: int, init_blocks: int = 1,
+                       local_blocks: int = 2, block_size: int = 64, kernel_stride: int = 16,
+                       policy: str = "bf16") -> Selection:
+    """The selection of given query rows of ONE sequence of ``seq_len`` tokens.
 
-    Same math as :func:`lightweight_compressed_attention` restricted to
-    ``rows`` (relative positions), so the long BASELINE configurations can be
-    checked on a sample without scoring every row.  ``take`` is the output
-    width (``min(topk, P)`` for a single sequence).
+    ``q_rows [R, H, D]`` are the queries at ``positions`` (relative, length
+    ``R``); ``kc [A, G, D]`` are all atoms of the sequence.  Same math as
+    :func:`lightweight_compressed_attention` restricted to those rows, so the
+    long BASELINE configurations can be checked (and timed on the CPU) on a
+    sample without scoring every row.  ``take`` is the output width.
     """
-    rows = np.asarray(rows, dtype=np.int64)
-    n = q.shape[0]
+    positions = np.asarray(positions, dtype=np.int64)
     q_fused, kv_fused = fold_weights(params, policy)
-    qs = project_queries(q[rows], q_fused, params.num_kv_heads, policy)
+    qs = project_queries(q_rows, q_fused, params.num_kv_heads, policy)
     ks = project_atom_keys(kc, kv_fused, policy)
-    pages = pool_atoms_to_pages(atom_scores(qs, ks), n, block_size, kernel_stride)
+    pages = pool_atoms_to_pages(atom_scores(qs, ks), seq_len, block_size, kernel_stride)
     g, r, p = pages.shape
-    qpage = rows // block_size
+    qpage = positions // block_size
     page_ids = np.arange(p)
     visible = page_ids[None, :] <= qpage[:, None]
     local = visible & (page_ids[None, :] + local_blocks >= qpage[:, None])
@@ -618,3 +623,70 @@ def select_rows(q: np.ndarray, kc: np.ndarray, params: SelectorParams, rows, *, 
     finite_vals = np.where(valid & np.isfinite(vals), vals, POS_INF)
     boundary = np.where(valid.any(-1), finite_vals.min(-1), np.nan).astype(np.float32)
     return Selection(idx, boundary, [(0, masked)])
+
+
+def select_rows(q: np.ndarray, kc: np.ndarray, params: SelectorParams, rows, *, take: int,
+                init_blocks: int = 1, local_blocks: int = 2, block_size: int = 64,
+                kernel_stride: int = 16, policy: str = "bf16") -> Selection:
+    """:func:`select_for_queries` for ``rows`` of a full ``q [N, H, D]``."""
+    rows = np.asarray(rows, dtype=np.int64)
+    return select_for_queries(q[rows], rows, q.shape[0], kc, params, take=take,
+                              init_blocks=init_blocks, local_blocks=local_blocks,
+                              block_size=block_size, kernel_stride=kernel_stride, policy=policy)
+
+
+def attention_for_queries(q_rows: np.ndarray, positions, k: np.ndarray, v: np.ndarray,
+                          topk_rows: np.ndarray, *, softmax_scale: float | None = None,
+                          block_size: int = 64) -> np.ndarray:
+    """Causal sparse attention of given query rows of ONE sequence (prefill).
+
+    ``q_rows [R, H, D]`` at ``positions``; ``k``/``v [N, G, D]`` the whole
+    sequence; ``topk_rows [G, R, T]`` their page lists.  Same math as
+    :func:`sparse_attention`; returns ``[R, H, D]`` float32.
+    """
+    positions = np.asarray(positions, dtype=np.int64)
+    n, g, d = k.shape
+    h = q_rows.shape[1]
+    hg = h // g
+    scale = float(d) ** -0.5 if softmax_scale is None else float(softmax_scale)
+    out = np.zeros((len(positions), h, d), dtype=np.float32)
+    n_pages = page_count(n, block_size)
+    for i, t in enumerate(positions):
+        limit = min(n, int(t) + 1)
+        for gi in range(g):
+            pages = sorted(set(int(p) for p in topk_rows[gi, i] if 0 <= p < n_pages))
+            keys = [np.arange(p * block_size, min((p + 1) * block_size, limit))
+                    for p in pages if p * block_size < limit]
+            if not keys:
+                continue
+            kk = np.concatenate(keys)
+            qh = q_rows[i, gi * hg:(gi + 1) * hg].astype(np.float64)
+            s_ = (qh @ k[kk, gi].astype(np.float64).T) * scale
+            e = np.exp(s_ - s_.max(axis=-1, keepdims=True))
+            out[i, gi * hg:(gi + 1) * hg] = ((e @ v[kk, gi].astype(np.float64))
+                                            / e.sum(-1, keepdims=True)).astype(np.float32)
+    return out
+
+
+def synthetic_keys_and_sample(seq_len: int, rows, *, num_heads: int = 32, num_kv_heads: int = 2,
+                              head_dim: int = 128, router_heads: int = 32, router_dim: int = 4,
+                              hot_pages: int = 24, hot_shift: float = 0.5, block_size: int = 64,
+                              seed: int = 0):
+    """Config-0/1 distribution for one sequence, with queries only at ``rows``.
+
+    Returns ``(q_rows [R, H, D], k, v [N, G, D], params)`` rounded to bf16;
+    for CPU timing at long lengths without materialising every query.
+    """
+    rng = np.random.default_rng(seed)
+    k = rng.standard_normal((seq_len, num_kv_heads, head_dim), dtype=np.float32)
+    v = rng.standard_normal((seq_len, num_kv_heads, head_dim), dtype=np.float32)
+    q = rng.standard_normal((len(rows), num_heads, head_dim), dtype=np.float32)
+    u = rng.standard_normal(head_dim).astype(np.float32)
+    u /= np.linalg.norm(u)
+    pages = page_count(seq_len, block_size)
+    for g in range(num_kv_heads):
+        for p in rng.choice(pages, size=min(hot_pages, pages), replace=False):
+            k[int(p) * block_size:min(int(p + 1) * block_size, seq_len), g] += hot_shift * u
+    q += hot_shift * u
+    params = selector_params(num_heads, num_kv_heads, head_dim, router_heads, router_dim, rng)
+    return bf16_round(q), bf16_round(k), bf16_round(v), params

@@ -113,7 +113,8 @@ def test_compress_module_matches_reference_contract():
 
 def _ulp_close(actual, expected, frac=0.99):
     a, e = np.asarray(actual, np.float32), np.asarray(expected, np.float32)
-    np.testing.assert_allclose(a, e, rtol=2 ** -7, atol=1e-6)
+    # atol covers near-zero outputs where fp32 accumulation order decides the last ulp.
+    np.testing.assert_allclose(a, e, rtol=2 ** -7, atol=1e-5)
     assert np.mean(a == e) >= frac, np.mean(a == e)
 
 

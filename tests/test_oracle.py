@@ -249,3 +249,19 @@ def test_bf16_round_matches_torch():
     np.testing.assert_array_equal(ora.bf16_round(x), expect)
     bits = ora.to_bf16_bits(x)
     np.testing.assert_array_equal(ora.from_bf16_bits(bits), expect)
+
+
+def test_row_level_helpers_agree_with_full_oracle():
+    """select_for_queries / attention_for_queries restate the packed functions on rows."""
+    inp = ora.synthetic_layer([900], num_heads=8, num_kv_heads=2, head_dim=32, router_heads=4,
+                              router_dim=8, hot_pages=3, seed=17, bf16=True)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    full = ora.lightweight_compressed_attention(inp.q, kc, inp.cu_seqlens, cu_c, inp.params,
+                                                topk=9, policy="bf16")
+    rows = np.array([0, 5, 64, 300, 777, 899])
+    sub = ora.select_for_queries(inp.q[rows], rows, 900, kc, inp.params, take=9)
+    np.testing.assert_array_equal(sub.topk_idx, full.topk_idx[:, rows])
+    out, _ = ora.sparse_attention(inp.q, inp.k, inp.v, inp.cu_seqlens, inp.cu_seqlens,
+                                  full.topk_idx, rows=rows)
+    got = ora.attention_for_queries(inp.q[rows], rows, inp.k, inp.v, full.topk_idx[:, rows])
+    np.testing.assert_allclose(got, out[rows], rtol=1e-6, atol=1e-6)
