@@ -29,6 +29,7 @@
 #ifndef LEANSELECT_B200_H_
 #define LEANSELECT_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -141,18 +142,31 @@ int ls_score_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
                    int32_t kernel_stride, float* page_scores, int32_t* status, void* stream);
 
 /*
+ * ls_select_pages_workspace_bytes -- bytes of scratch ls_select_pages needs:
+ * the pooled page scores of every (group, query row), fp32, rows padded to
+ * 8 pages: 4 * G * total_q * round_up(ceil(max_seqlen_q / 64), 8).
+ */
+size_t ls_select_pages_workspace_bytes(int64_t total_q, int32_t num_kv_heads,
+                                       int32_t max_seqlen_q);
+
+/*
  * ls_select_pages -- replaces the selection loop of
  * MiniCPMInfLLMv2Attention._lightweight_compressed_attention
- * (leanselect/models/minicpm.py:3093-3141): fused Q projection, atom scoring,
- * page pooling, visibility/forced masking and streaming top-T in one
- * tcgen05 kernel.  Page scores are never written to HBM.
+ * (leanselect/models/minicpm.py:3093-3141).
+ *
+ * Two kernels: a tcgen05 kernel computes the Q projection, the atom scores
+ * and the page max-pool for every (group, row, candidate page) into
+ * `workspace`; a warp-per-row radix select then picks the pages.
  *
  * topk_idx [G, total_q, take] int32, take = min(topk, max_pages) as in the
- * reference (minicpm.py:3096-3104).  Row t of sequence b holds the forced
- * pages (p < init_blocks, and p in [t/64 - local_blocks, t/64]) followed by
- * the best-scoring visible non-forced pages, min(take, P_b) entries in all,
- * then -1.  Order within a row is unspecified (the reference uses
- * torch.topk(sorted=False)); ties are broken toward the lower page index.
+ * reference (minicpm.py:3096-3104).  Row t of sequence b holds
+ * min(take, P_b) pages -- the forced pages (p < init_blocks, and
+ * p in [t/64 - local_blocks, t/64]) and the best-scoring visible non-forced
+ * pages, in ascending page order -- then -1.  Ties are broken toward the
+ * lower page index (the reference uses torch.topk, whose order and
+ * tie-break are unspecified).  Rows of sequences without atoms are all -1
+ * (minicpm.py:3115-3116).  `workspace` must hold
+ * ls_select_pages_workspace_bytes(total_q, G, max_seqlen_q) bytes.
  * Requires take <= LS_MAX_TOPK, block_size == 64, kernel_stride == 16.
  */
 int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
@@ -160,7 +174,8 @@ int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
                     int32_t max_seqlen_q, int64_t total_q, int64_t total_c, int32_t num_heads,
                     int32_t num_kv_heads, int32_t head_dim, int32_t width, int32_t take,
                     int32_t init_blocks, int32_t local_blocks, int32_t block_size,
-                    int32_t kernel_stride, int32_t* topk_idx, int32_t* status, void* stream);
+                    int32_t kernel_stride, int32_t* topk_idx, void* workspace,
+                    size_t workspace_bytes, int32_t* status, void* stream);
 
 /*
  * ls_select_pages_chunk -- ls_select_pages for a slice of ONE sequence, used
@@ -168,14 +183,16 @@ int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
  * prefill runs on one GPU).  q holds chunk_q query rows at positions
  * [q_position, q_position + chunk_q) of a sequence of seq_len tokens whose
  * total_c atoms are all of ks [G, total_c, F].  Visibility, forced pages and
- * the output width `take` follow ls_select_pages with P = ceil(seq_len/64).
+ * the output width `take` follow ls_select_pages with P = ceil(seq_len/64);
+ * `workspace` holds ls_select_pages_workspace_bytes(chunk_q, G, seq_len) bytes.
  */
 int ls_select_pages_chunk(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
                           int64_t chunk_q, int32_t q_position, int32_t seq_len, int64_t total_c,
                           int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t width,
                           int32_t take, int32_t init_blocks, int32_t local_blocks,
                           int32_t block_size, int32_t kernel_stride, int32_t* topk_idx,
-                          int32_t* status, void* stream);
+                          void* workspace, size_t workspace_bytes, int32_t* status,
+                          void* stream);
 
 /*
  * ls_sparse_attn -- replaces infllmv2_attn_varlen_func(..., topk_idx=)

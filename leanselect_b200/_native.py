@@ -28,6 +28,7 @@ _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
 _F32 = ctypes.c_float
+_SZ = ctypes.c_size_t
 
 # name -> argument types (all return int), in header order.
 SIGNATURES = {
@@ -39,13 +40,17 @@ SIGNATURES = {
     "ls_score_pages": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _I32,
                        _I32, _P, _P, _P],
     "ls_select_pages": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _I32,
-                        _I32, _I32, _I32, _I32, _P, _P, _P],
+                        _I32, _I32, _I32, _I32, _P, _P, _SZ, _P, _P],
     "ls_select_pages_chunk": [_P, _P, _P, _I64, _I32, _I32, _I64, _I32, _I32, _I32, _I32, _I32,
-                              _I32, _I32, _I32, _I32, _P, _P, _P],
+                              _I32, _I32, _I32, _I32, _P, _P, _SZ, _P, _P],
+    "ls_bb_rms_norm": [_P, _P, _I64, _I32, _F32, _P, _P],
+    "ls_bb_rope_split": [_P, _P, _P, _F32, _I64, _I32, _I32, _I32, _P, _P, _P, _P],
+    "ls_bb_silu_mul": [_P, _I64, _I32, _P, _P],
     "ls_sparse_attn": [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _P,
                        _I32, _I32, _F32, _I32, _P, _P, _P, _P],
 }
 STRING_FUNCS = ("ls_status_string", "ls_last_error", "ls_version")
+SIZE_FUNCS = {"ls_select_pages_workspace_bytes": [_I64, _I32, _I32]}
 
 _lock = threading.Lock()
 _lib = None
@@ -81,6 +86,10 @@ def load(path: os.PathLike | str | None = None) -> ctypes.CDLL:
         lib.ls_last_error.restype = ctypes.c_char_p
         lib.ls_version.argtypes = []
         lib.ls_version.restype = ctypes.c_char_p
+        for name, argtypes in SIZE_FUNCS.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = ctypes.c_size_t
         if path is None:
             _lib = lib
         return lib

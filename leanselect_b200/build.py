@@ -21,7 +21,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "_lib"
 LIB = LIB_DIR / "libleanselect_b200.so"
-SOURCES = ["prep.cu", "score_select.cu", "sparse_attn.cu", "capi.cu"]
+SOURCES = ["prep.cu", "score_select.cu", "sparse_attn.cu", "capi.cu", "backbone.cu"]
 HEADERS = ["common.cuh", "launch.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -40,8 +40,8 @@ def _stale() -> bool:
     if not LIB.exists():
         return True
     built = LIB.stat().st_mtime
-    inputs = [CSRC / s for s in SOURCES + HEADERS] + [ROOT / "include" / "leanselect_b200.h",
-                                                       Path(__file__)]
+    inputs = [CSRC / s for s in SOURCES + HEADERS] + sorted((ROOT / "include").glob("*.h")) + [
+        Path(__file__)]
     return any(p.stat().st_mtime > built for p in inputs)
 
 

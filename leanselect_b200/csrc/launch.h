@@ -47,12 +47,16 @@ struct ScoreArgs {
   int pos_offset;      // chunk mode: position of query row 0 inside its sequence
   int seq_len;         // chunk mode: length of the whole sequence (0 = rows are the sequence)
   int32_t* topk_idx;   // kModeSelect
+  float* workspace;    // kModeSelect: pooled page scores [G, total_q, round8(max_pages)]
   float* page_scores;  // kModeScore
   uint16_t* qs_out;    // kModeProject: [G, total_q, F] bf16
   int32_t* status;
 };
 
 cudaError_t launch_score(int mode, const ScoreArgs& args, cudaStream_t stream);
+
+// Floats of selection workspace for `rows` = G * query rows and `max_pages`.
+size_t select_workspace_floats(int64_t rows, int max_pages);
 
 // Sparse attention (sparse_attn.cu).
 struct AttnArgs {

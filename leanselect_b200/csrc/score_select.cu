@@ -1,26 +1,38 @@
 // Selector scoring and page selection on the 5th-generation tensor cores.
 //
-// One CTA owns a tile of 128 query rows of one sequence and one KV group.
+// score_kernel: one CTA owns a tile of 128 query rows of one sequence and one
+// KV group.
 //
 //   Phase A  Qs = Q_tile[128, Hg*D] x WqT_g[F, Hg*D]^T            (a3, selector.py:160-177)
-//            TMA streams 64-wide K blocks of Q and WqT through a 3-stage ring,
+//            TMA streams 64-wide K blocks of Q and WqT through a 2-stage ring,
 //            one thread issues tcgen05.mma (M=128, N=128, K=16) into TMEM.
 //            The epilogue warps round Qs to bf16 (the reference's bf16 einsum
 //            output) and store it back to shared memory as the A operand of
 //            phase B (128B-swizzled K-major, the layout TMA would write).
 //   Phase B  for each tile of 128 atoms: S = Qs x Ks_tile^T        (a5, selector.py:203-207)
-//            into one of two TMEM accumulators (double buffered), while the
-//            epilogue warps drain the other: each thread owns one query row,
-//            max-pools atoms into pages (window 5, stride 4, pad 1; a6,
-//            pages.py:146-187) and either writes the page scores (score
-//            mode) or feeds visible non-forced pages into a per-row min-heap
-//            of the best T' pages in shared memory (select mode; a7,
-//            minicpm.py:3124-3141).  Only atom tiles that can reach a
-//            candidate page are computed: the atom loop stops at the causal
-//            limit of the tile's last row.
+//            into one of two TMEM accumulators (double buffered; buffer 0
+//            reuses the drained Qs columns), while the epilogue warps drain
+//            the other: each thread owns one query row and max-pools atoms
+//            into pages (window 5, stride 4, pad 1; a6, pages.py:146-187),
+//            32 pages per atom tile, written as fp32 either to the caller's
+//            page-score output (score mode) or to the selection workspace
+//            (select mode).  In select mode only the atom tiles that can
+//            reach a candidate page of the tile's last row are computed.
 //
-// Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
-// owner, warps 2-5 epilogue (warp w reads TMEM lanes 32*(w%4) .. +31).
+// topk_kernel (select mode, a7 minicpm.py:3124-3141): one warp per (group,
+// query row) reads the row's candidate pages (visible, not forced) from the
+// workspace and finds the best T' = min(take_b, P_b) - forced by an exact
+// MSB-first radix select on order-preserving 32-bit keys (4 passes of 8
+// bits, histograms in shared memory), breaking ties toward the lower page.
+// It writes sink pages, selected pages and local pages -- ascending -- then
+// -1 padding.
+//
+// Warp roles of score_kernel (192 threads): warp 0 TMA producer, warp 1 MMA
+// issuer and TMEM owner, warps 2-5 epilogue (warp w reads TMEM lanes
+// 32*(w%4) .. +31).  Two CTAs fit on an SM (shared memory and 256 TMEM
+// columns each), so one CTA's phase A overlaps another's phase B.
+#include <algorithm>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -29,12 +41,10 @@ namespace {
 
 constexpr int kRows = 128;
 constexpr int kWidth = 128;          // F
-constexpr int kStages = 3;
+constexpr int kStages = 2;
 constexpr int kHalfBytes = 128 * 128;        // [128 rows x 64 bf16]
 constexpr int kStageBytes = 2 * kHalfBytes;  // A+B (phase A) or one Ks tile (phase B)
 constexpr int kQsBytes = 2 * kHalfBytes;
-constexpr int kHeapCap = LS_MAX_TOPK;
-constexpr int kHeapBytes = kHeapCap * kRows * (4 + 2);
 constexpr int kThreads = 192;
 constexpr uint32_t kIdesc = umma_idesc_bf16(128, 128);
 
@@ -53,13 +63,13 @@ struct Barriers {
 __host__ __device__ constexpr size_t smem_bytes(int mode) {
   return 1024  // alignment slack
          + static_cast<size_t>(kStages) * kStageBytes + (mode == kModeProject ? 0 : kQsBytes) +
-         (mode == kModeSelect ? kHeapBytes : 0) + sizeof(Barriers);
+         sizeof(Barriers);
 }
 
 struct TileInfo {
   int g, b, tile;
   int64_t q0;       // first packed query row of the sequence
-  int n;            // sequence length
+  int n;            // query rows of the sequence
   int row0;         // first row of the tile inside the sequence
   int rows;         // valid rows in the tile
   int64_t c0;       // first packed atom of the sequence
@@ -70,12 +80,8 @@ struct TileInfo {
   bool prologue;    // whether Qs is computed at all
 };
 
-__device__ __forceinline__ bool worse(float sa, uint32_t pa, float sb, uint32_t pb) {
-  return sa < sb || (sa == sb && pa > pb);
-}
-
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constant__ ScoreArgs args) {
+__global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constant__ ScoreArgs args) {
   const int tiles_max = (args.max_seqlen_q + kRows - 1) / kRows;
   TileInfo ti;
   {
@@ -83,7 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constan
     ti.g = static_cast<int>(i % args.num_groups);
     ti.b = static_cast<int>((i / args.num_groups) % args.batch);
     ti.tile = tiles_max - 1 - static_cast<int>(i / (static_cast<int64_t>(args.num_groups) * args.batch));
-    // Null cu_seqlens (projection only): all rows form one sequence.
+    // Null cu_seqlens (projection, chunk mode): all rows form one sequence.
     ti.q0 = args.cu_q ? __ldg(args.cu_q + ti.b) : 0;
     ti.n = args.cu_q ? static_cast<int>(__ldg(args.cu_q + ti.b + 1) - ti.q0) : args.max_seqlen_q;
     ti.row0 = ti.tile * kRows;
@@ -109,16 +115,28 @@ __global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constan
     ti.atom_tiles = (needed_atoms + kRows - 1) / kRows;
     ti.prologue = (MODE == kModeProject) || ti.atom_tiles > 0;
   }
+  // Select mode: a tile without candidate pages has nothing to score
+  // (such rows have no candidates, so the top-k kernel reads nothing).
+  // Score mode: a sequence without atoms scores -inf everywhere.
+  if (!ti.prologue) {
+    if (MODE == kModeScore) {
+      const int64_t count = static_cast<int64_t>(ti.rows) * args.max_pages;
+      for (int64_t i = threadIdx.x; i < count; i += blockDim.x) {
+        const int64_t q_row = ti.q0 + ti.row0 + i / args.max_pages;
+        args.page_scores[(static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_pages +
+                         i % args.max_pages] = -INFINITY;
+      }
+    }
+    return;
+  }
 
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* stages = smem;
   uint8_t* qs_smem = stages + kStages * kStageBytes;
-  uint8_t* heap_base = qs_smem + (MODE == kModeProject ? 0 : kQsBytes);
-  float* heap_s = reinterpret_cast<float*>(heap_base);
-  uint16_t* heap_p = reinterpret_cast<uint16_t*>(heap_base + kHeapCap * kRows * 4);
-  Barriers* bars = reinterpret_cast<Barriers*>(heap_base + (MODE == kModeSelect ? kHeapBytes : 0));
+  Barriers* bars =
+      reinterpret_cast<Barriers*>(qs_smem + (MODE == kModeProject ? 0 : kQsBytes));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -138,14 +156,13 @@ __global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constan
     bars->abort_flag = 0;
     fence_barrier_init();
   }
-  const uint32_t tmem_cols = MODE == kModeProject ? 128 : 512;
+  const uint32_t tmem_cols = MODE == kModeProject ? 128 : 256;
   if (warp == 1) tmem_alloc(&bars->tmem_base, tmem_cols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t tmem_qs = tmem;          // columns [0, 128)
-  const uint32_t tmem_s = tmem + 128;     // columns [128, 384): two 128-column buffers
+  const uint32_t tmem_qs = tmem;  // columns [0, 128); reused as S buffer 0 in phase B
   volatile int* abort_flag = &bars->abort_flag;
   int32_t* status = args.status;
 
@@ -160,17 +177,15 @@ __global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constan
       if (MODE != kModeProject) tma_prefetch_desc(&args.tm_ks);
       int it = 0;
       bool ok = true;
-      if (ti.prologue) {
-        const int32_t qrow = static_cast<int32_t>(ti.q0 + ti.row0);
-        for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
-          const int s = it % kStages;
-          ok = mbar_wait(&bars->empty[s], ((it / kStages) & 1) ^ 1, status, abort_flag);
-          if (!ok) break;
-          uint8_t* st = stages + s * kStageBytes;
-          mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
-          tma_load_2d(st, &args.tm_q, &bars->full[s], ti.g * kd + kb * 64, qrow);
-          tma_load_2d(st + kHalfBytes, &args.tm_w, &bars->full[s], kb * 64, ti.g * kWidth);
-        }
+      const int32_t qrow = static_cast<int32_t>(ti.q0 + ti.row0);
+      for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
+        const int s = it % kStages;
+        ok = mbar_wait(&bars->empty[s], ((it / kStages) & 1) ^ 1, status, abort_flag);
+        if (!ok) break;
+        uint8_t* st = stages + s * kStageBytes;
+        mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+        tma_load_2d(st, &args.tm_q, &bars->full[s], ti.g * kd + kb * 64, qrow);
+        tma_load_2d(st + kHalfBytes, &args.tm_w, &bars->full[s], kb * 64, ti.g * kWidth);
       }
       if (MODE != kModeProject) {
         for (int j = 0; j < ti.atom_tiles && ok; ++j, ++it) {
@@ -196,23 +211,22 @@ __global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constan
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      if (ti.prologue) {
-        for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
-          const int s = it % kStages;
-          ok = mbar_wait(&bars->full[s], (it / kStages) & 1, status, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t a = smem_u32(stages + s * kStageBytes);
-          const uint32_t b = a + kHalfBytes;
+      for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
+        const int s = it % kStages;
+        ok = mbar_wait(&bars->full[s], (it / kStages) & 1, status, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(stages + s * kStageBytes);
+        const uint32_t b = a + kHalfBytes;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16_ss(tmem_qs, umma_desc_sw128(a + kk * 32), umma_desc_sw128(b + kk * 32),
-                         kIdesc, (kb | kk) != 0);
-          umma_commit(&bars->empty[s]);
-        }
-        umma_commit(&bars->qs_full);
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16_ss(tmem_qs, umma_desc_sw128(a + kk * 32), umma_desc_sw128(b + kk * 32),
+                       kIdesc, (kb | kk) != 0);
+        umma_commit(&bars->empty[s]);
       }
-      if (MODE != kModeProject && ok && ti.atom_tiles > 0) {
+      umma_commit(&bars->qs_full);
+      if (MODE != kModeProject && ok) {
+        // Qs has been drained from TMEM and stored to shared memory.
         ok = mbar_wait(&bars->qs_ready, 0, status, abort_flag);
         tc_fence_after();
         const uint32_t qa = smem_u32(qs_smem);
@@ -228,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constan
           for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              umma_bf16_ss(tmem_s + buf * 128, umma_desc_sw128(qa + h * kHalfBytes + kk * 32),
+              umma_bf16_ss(tmem + buf * 128, umma_desc_sw128(qa + h * kHalfBytes + kk * 32),
                            umma_desc_sw128(kb_addr + h * kHalfBytes + kk * 32), kIdesc,
                            (h | kk) != 0);
           umma_commit(&bars->empty[s]);
@@ -244,62 +258,47 @@ __global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constan
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const bool valid = row < ti.rows;
-    const int t_rel = ti.pos0 + ti.row0 + row;       // position inside the sequence
     const int64_t q_row = ti.q0 + ti.row0 + row;     // packed row
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-    bool ok = true;
-
-    // Per-row selection geometry (minicpm.py:3121-3138).
-    const int qp = t_rel / 64;
-    const int take_b = min(args.take, ti.pages);
-    const int n_init = min(args.init_blocks, qp + 1);      // visible sink pages 0 .. n_init-1
-    const int lo = max(0, qp - args.local_blocks);          // local pages lo .. qp
-    const int overlap = max(0, n_init - lo);
-    const int n_forced = n_init + (qp - lo + 1) - overlap;
-    const int n_cand = max(0, lo - n_init);                 // visible non-forced pages n_init .. lo-1
-    const int cap = max(0, min(take_b - n_forced, n_cand));
-    int hsize = 0;
-
-    if (ti.prologue) {
-      ok = mbar_wait(&bars->qs_full, 0, status, abort_flag);
-      tc_fence_after();
-      if (ok) {
+    bool ok = mbar_wait(&bars->qs_full, 0, status, abort_flag);
+    tc_fence_after();
+    if (ok) {
 #pragma unroll 1
-        for (int q = 0; q < 4; ++q) {
-          float v[32];
-          tmem_ld32(tmem_qs + lane_base + q * 32, v);
-          uint4 packed[4];
+      for (int q = 0; q < 4; ++q) {
+        float v[32];
+        tmem_ld32(tmem_qs + lane_base + q * 32, v);
+        uint4 packed[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          packed[c].x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
+          packed[c].y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
+          packed[c].z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
+          packed[c].w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
+        }
+        if (MODE == kModeProject) {
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(
+                args.qs_out + (static_cast<int64_t>(ti.g) * args.total_q + q_row) * kWidth + q * 32);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) dst[c] = packed[c];
+          }
+        } else {
+          uint8_t* half = qs_smem + (q >> 1) * kHalfBytes + row * 128;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            packed[c].x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
-            packed[c].y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
-            packed[c].z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
-            packed[c].w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
-          }
-          if (MODE == kModeProject) {
-            if (valid) {
-              uint4* dst = reinterpret_cast<uint4*>(
-                  args.qs_out + (static_cast<int64_t>(ti.g) * args.total_q + q_row) * kWidth + q * 32);
-#pragma unroll
-              for (int c = 0; c < 4; ++c) dst[c] = packed[c];
-            }
-          } else {
-            uint8_t* half = qs_smem + (q >> 1) * kHalfBytes + row * 128;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const int chunk = (q & 1) * 4 + c;
-              *reinterpret_cast<uint4*>(half + ((chunk ^ (row & 7)) << 4)) = packed[c];
-            }
+            const int chunk = (q & 1) * 4 + c;
+            *reinterpret_cast<uint4*>(half + ((chunk ^ (row & 7)) << 4)) = packed[c];
           }
         }
       }
-      if (MODE != kModeProject) {
-        fence_proxy_async_smem();
-        mbar_arrive(&bars->qs_ready);
-      }
     }
-
     if (MODE != kModeProject) {
+      tc_fence_before();
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->qs_ready);
+
+      float* out_row = (MODE == kModeScore ? args.page_scores : args.workspace) +
+                       (static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_pages;
       float carry = -INFINITY;  // score of the last atom of the previous tile
       const int last_atom = ti.atoms - 1;
       for (int j = 0; j < ti.atom_tiles && ok; ++j) {
@@ -310,81 +309,48 @@ __global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constan
 #pragma unroll 1
         for (int q = 0; q < 4; ++q) {
           float v[32];
-          tmem_ld32(tmem_s + buf * 128 + lane_base + q * 32, v);
+          tmem_ld32(tmem + buf * 128 + lane_base + q * 32, v);
           const int a_base = j * 128 + q * 32;
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             if (a_base + i > last_atom) v[i] = -INFINITY;
+          float pg[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            float m = i == 0 ? carry : v[4 * i - 1];
-            m = fmaxf(m, fmaxf(fmaxf(v[4 * i], v[4 * i + 1]), fmaxf(v[4 * i + 2], v[4 * i + 3])));
-            const int p = j * 32 + q * 8 + i;
-            if (MODE == kModeScore) {
-              if (valid && p < args.max_pages)
-                args.page_scores[(static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_pages + p] =
-                    p < ti.pages ? m : -INFINITY;
-            } else {
-              // Candidate: visible, not forced, finite.
-              if (valid && p >= n_init && p < lo && m > -INFINITY && cap > 0) {
-                if (hsize < cap) {
-                  int k = hsize++;
-                  while (k > 0) {
-                    const int parent = (k - 1) >> 1;
-                    const float ps = heap_s[parent * kRows + row];
-                    const uint32_t pp = heap_p[parent * kRows + row];
-                    if (!worse(m, p, ps, pp)) break;
-                    heap_s[k * kRows + row] = ps;
-                    heap_p[k * kRows + row] = static_cast<uint16_t>(pp);
-                    k = parent;
-                  }
-                  heap_s[k * kRows + row] = m;
-                  heap_p[k * kRows + row] = static_cast<uint16_t>(p);
-                } else if (m > heap_s[row]) {
-                  int k = 0;
-                  while (true) {
-                    const int l = 2 * k + 1;
-                    if (l >= hsize) break;
-                    int c = l;
-                    float cs = heap_s[l * kRows + row];
-                    uint32_t cp = heap_p[l * kRows + row];
-                    if (l + 1 < hsize) {
-                      const float rs = heap_s[(l + 1) * kRows + row];
-                      const uint32_t rp = heap_p[(l + 1) * kRows + row];
-                      if (worse(rs, rp, cs, cp)) { c = l + 1; cs = rs; cp = rp; }
-                    }
-                    if (!worse(cs, cp, m, p)) break;
-                    heap_s[k * kRows + row] = cs;
-                    heap_p[k * kRows + row] = static_cast<uint16_t>(cp);
-                    k = c;
-                  }
-                  heap_s[k * kRows + row] = m;
-                  heap_p[k * kRows + row] = static_cast<uint16_t>(p);
-                }
-              }
-            }
+            const float m = i == 0 ? carry : v[4 * i - 1];
+            pg[i] = fmaxf(m, fmaxf(fmaxf(v[4 * i], v[4 * i + 1]), fmaxf(v[4 * i + 2], v[4 * i + 3])));
           }
           carry = v[31];
+          const int p0 = j * 32 + q * 8;
+          if (valid && p0 < args.max_pages) {
+            if (MODE == kModeScore) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                if (p0 + i >= ti.pages) pg[i] = -INFINITY;
+            }
+            if ((args.max_pages & 7) == 0) {
+              // Workspace rows (select mode) are padded to 8 pages: 32-byte stores.
+              *reinterpret_cast<float4*>(out_row + p0) = make_float4(pg[0], pg[1], pg[2], pg[3]);
+              *reinterpret_cast<float4*>(out_row + p0 + 4) = make_float4(pg[4], pg[5], pg[6], pg[7]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                if (p0 + i < args.max_pages) out_row[p0 + i] = pg[i];
+            }
+          }
         }
         tc_fence_before();
         mbar_arrive(&bars->s_empty[buf]);
       }
-      if (MODE == kModeScore && valid) {
-        // Pages past the last computed tile: only page 32*tiles can still see an atom.
-        for (int p = ti.atom_tiles * 32; p < args.max_pages; ++p)
-          args.page_scores[(static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_pages + p] =
-              (p == ti.atom_tiles * 32 && p < ti.pages) ? carry : -INFINITY;
-      }
-      if (MODE == kModeSelect && valid) {
-        int32_t* out = args.topk_idx + (static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.take;
-        int k = 0;
-        if (ti.atoms > 0) {
-          // Forced pages first (sink pages, then local pages), lowest index first.
-          for (int p = 0; p < n_init && k < take_b; ++p) out[k++] = p;
-          for (int p = max(lo, n_init); p <= qp && k < take_b; ++p) out[k++] = p;
-          for (int i = 0; i < hsize; ++i) out[k++] = heap_p[i * kRows + row];
-        }
-        for (; k < args.take; ++k) out[k] = -1;
+      if (valid && ok) {
+        // Pages past the last computed tile: only page 32*tiles can still see
+        // an atom (the last one, carried).  Score mode fills the whole row;
+        // select mode fills up to the row's last candidate page.
+        const int qp = (ti.pos0 + ti.row0 + row) / 64;
+        const int end = MODE == kModeScore ? args.max_pages
+                                           : min(args.max_pages, qp - args.local_blocks);
+        for (int p = ti.atom_tiles * 32; p < end; ++p)
+          out_row[p] = (p == ti.atom_tiles * 32 && p < ti.pages) ? carry : -INFINITY;
       }
     }
   }
@@ -397,9 +363,163 @@ __global__ void __launch_bounds__(kThreads, 1) score_kernel(const __grid_constan
   }
 }
 
+// ---------------------------------------------------------------------------
+// Top-T' page selection per (group, row)
+// ---------------------------------------------------------------------------
+
+constexpr int kTopkWarps = 8;
+
+// Order-preserving map of fp32 to uint32; -inf and NaN map to 0 (never picked).
+__device__ __forceinline__ uint32_t score_key(float s) {
+  if (!(s > -INFINITY)) return 0u;  // -inf or NaN
+  const uint32_t u = __float_as_uint(s);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_constant__ ScoreArgs args) {
+  __shared__ uint32_t hist_all[kTopkWarps][256];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  uint32_t* hist = hist_all[warp];
+  const int64_t rows_total = static_cast<int64_t>(args.num_groups) * args.total_q;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kTopkWarps + warp; r < rows_total;
+       r += static_cast<int64_t>(gridDim.x) * kTopkWarps) {
+    const int64_t q_row = r % args.total_q;
+    int b = 0, n;
+    int64_t q0 = 0;
+    if (args.cu_q) {
+      b = find_sequence(args.cu_q, args.batch, q_row);
+      q0 = __ldg(args.cu_q + b);
+      n = static_cast<int>(__ldg(args.cu_q + b + 1) - q0);
+    } else {
+      n = args.max_seqlen_q;
+    }
+    const int atoms = args.cu_c ? static_cast<int>(__ldg(args.cu_c + b + 1) - __ldg(args.cu_c + b))
+                                : static_cast<int>(args.total_c);
+    const int pos = args.pos_offset + static_cast<int>(q_row - q0);
+    const int pages = ((args.seq_len > 0 ? args.seq_len : n) + 63) / 64;
+    int32_t* out = args.topk_idx + r * args.take;
+    const float* scores = args.workspace + r * args.max_pages;
+
+    // Row geometry (minicpm.py:3121-3138).
+    const int qp = pos / 64;
+    const int take_b = min(args.take, pages);
+    const int n_init = min(args.init_blocks, qp + 1);   // sink pages 0 .. n_init-1
+    const int lo = max(0, qp - args.local_blocks);       // local pages lo .. qp
+    const int local0 = max(lo, n_init);
+    const int n_local = qp - local0 + 1;                 // local pages that are not sinks
+    const int n_forced = n_init + n_local;
+    const int m = max(0, lo - n_init);                   // candidates n_init .. lo-1
+    const int cap = max(0, min(take_b - n_forced, m));
+    if (atoms <= 0) {
+      // The reference leaves rows of sequences without atoms at -1 (minicpm.py:3115-3116).
+      for (int k = lane; k < args.take; k += 32) out[k] = -1;
+      continue;
+    }
+    const int sinks_out = min(n_init, take_b);
+    for (int k = lane; k < sinks_out; k += 32) out[k] = k;
+
+    // ---- threshold key by MSB-first radix select over the candidates.
+    uint32_t prefix = 0, mask = 0;
+    int need = cap;
+    int valid_total = 0;
+    if (cap > 0) {
+      // Count finite candidates first: if all fit, no selection is needed.
+      for (int i = lane; i < m; i += 32) valid_total += score_key(scores[n_init + i]) != 0u;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) valid_total += __shfl_xor_sync(0xffffffffu, valid_total, o);
+    }
+    const bool select_all = valid_total <= cap;
+    if (cap > 0 && !select_all) {
+#pragma unroll 1
+      for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int k = lane; k < 256; k += 32) hist[k] = 0;
+        __syncwarp();
+        for (int i = lane; i < m; i += 32) {
+          const uint32_t key = score_key(scores[n_init + i]);
+          if (key != 0u && ((key ^ prefix) & mask) == 0) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncwarp();
+        // Lane l owns bins 255-8l .. 248-8l (descending).
+        uint32_t c[8];
+        uint32_t lane_sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          c[j] = hist[255 - 8 * lane - j];
+          lane_sum += c[j];
+        }
+        uint32_t incl = lane_sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const uint32_t excl = incl - lane_sum;
+        const bool here = excl < static_cast<uint32_t>(need) && incl >= static_cast<uint32_t>(need);
+        const uint32_t owner_mask = __ballot_sync(0xffffffffu, here);
+        const int owner = __ffs(owner_mask) - 1;
+        int bin = 0;
+        uint32_t above = 0;
+        if (here) {
+          uint32_t cum = excl;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (cum + c[j] >= static_cast<uint32_t>(need)) {
+              bin = 255 - 8 * lane - j;
+              above = cum;
+              break;
+            }
+            cum += c[j];
+          }
+        }
+        bin = __shfl_sync(0xffffffffu, bin, owner);
+        above = __shfl_sync(0xffffffffu, above, owner);
+        need -= static_cast<int>(above);
+        prefix |= static_cast<uint32_t>(bin) << shift;
+        mask |= 0xFFu << shift;
+        __syncwarp();
+      }
+    }
+    // ---- emit candidates in page order: keys above the threshold, plus the
+    // first `need` keys equal to it (lower pages first).
+    int k_out = sinks_out;
+    if (cap > 0) {
+      int ties_seen = 0;
+      for (int base = 0; base < m; base += 32) {
+        const int i = base + lane;
+        const uint32_t key = i < m ? score_key(scores[n_init + i]) : 0u;
+        bool take;
+        if (select_all) {
+          take = key != 0u;
+        } else {
+          const bool tie = key == prefix;
+          const uint32_t tie_mask = __ballot_sync(0xffffffffu, tie);
+          const int tie_rank = ties_seen + __popc(tie_mask & ((1u << lane) - 1));
+          take = key > prefix || (tie && tie_rank < need);
+          ties_seen += __popc(tie_mask);
+        }
+        const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
+        if (take) out[k_out + __popc(take_mask & ((1u << lane) - 1))] = n_init + i;
+        k_out += __popc(take_mask);
+      }
+    }
+    // Local pages (those that are not sinks), then padding.
+    const int local_out = max(0, min(n_local, take_b - k_out));
+    for (int k = lane; k < local_out; k += 32) out[k_out + k] = local0 + k;
+    k_out += local_out;
+    for (int k = k_out + lane; k < args.take; k += 32) out[k] = -1;
+  }
+}
+
 }  // namespace
 
-cudaError_t launch_score(int mode, const ScoreArgs& args, cudaStream_t stream) {
+size_t select_workspace_floats(int64_t rows, int max_pages) {
+  return static_cast<size_t>(rows) * static_cast<size_t>((max_pages + 7) & ~7);
+}
+
+cudaError_t launch_score(int mode, const ScoreArgs& args_in, cudaStream_t stream) {
+  ScoreArgs args = args_in;
   const int tiles_max = (args.max_seqlen_q + kRows - 1) / kRows;
   const int64_t grid = static_cast<int64_t>(tiles_max) * args.batch * args.num_groups;
   if (grid == 0) return cudaSuccess;
@@ -418,18 +538,24 @@ cudaError_t launch_score(int mode, const ScoreArgs& args, cudaStream_t stream) {
       if (err != cudaSuccess) return err;
       score_kernel<kModeScore><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
       break;
-    case kModeSelect:
+    case kModeSelect: {
+      // Workspace rows are padded to a multiple of 8 pages (32-byte aligned stores).
+      args.max_pages = (args.max_pages + 7) & ~7;
       err = cudaFuncSetAttribute(score_kernel<kModeSelect>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
       if (err != cudaSuccess) return err;
       score_kernel<kModeSelect><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
+      err = cudaGetLastError();
+      if (err != cudaSuccess) return err;
+      const int64_t rows = static_cast<int64_t>(args.num_groups) * args.total_q;
+      const int64_t blocks = std::min<int64_t>((rows + kTopkWarps - 1) / kTopkWarps, 148 * 16);
+      topk_kernel<<<static_cast<unsigned>(blocks), kTopkWarps * 32, 0, stream>>>(args);
       break;
+    }
     default:
       return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
 }
-
-size_t score_smem_bytes(int mode) { return smem_bytes(mode); }
 
 }  // namespace ls

@@ -19,10 +19,11 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass, field
-from typing import Callable, Sequence
+from typing import Sequence
 
 import torch
 
+from . import host_kernels as hk
 from .attention import LayerConfig, count_attended_keys, prefill_layer_attention
 from .selector import LeanSelectSelector
 
@@ -63,13 +64,14 @@ class MiniCPMShape:
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """Torch reference of the fused RMSNorm kernel (minicpm.py:772-798)."""
     xf = x.float()
     xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
     return (xf * weight.float()).to(x.dtype)
 
 
 class LongRoPE:
-    """Rotary tables with LongRoPE frequency divisors (minicpm.py:895-940)."""
+    """Rotary frequencies with LongRoPE divisors (minicpm.py:895-940)."""
 
     def __init__(self, shape: MiniCPMShape, device: torch.device, seed: int = 0):
         d = shape.head_dim
@@ -83,16 +85,20 @@ class LongRoPE:
         scale = shape.max_position / shape.original_max_position
         self.scaling = math.sqrt(1 + math.log(scale) / math.log(self.orig)) if scale > 1 else 1.0
 
-    def tables(self, positions: torch.Tensor, seq_len: int):
-        """``cos, sin [N, D]`` (bf16) for integer ``positions``."""
+    def frequencies(self, seq_len: int) -> torch.Tensor:
+        """Per-frequency inverse wavelengths for a sequence of ``seq_len`` tokens."""
         ext = self.long_factor if seq_len > self.orig else torch.ones_like(self.long_factor)
-        freqs = positions.float()[:, None] * (self.inv_freq / ext)[None, :]
+        return self.inv_freq / ext
+
+    def tables(self, positions: torch.Tensor, seq_len: int):
+        """``cos, sin [N, D]`` (fp32, scaled) for integer ``positions`` (torch reference)."""
+        freqs = positions.float()[:, None] * self.frequencies(seq_len)[None, :]
         emb = torch.cat((freqs, freqs), dim=-1)
-        return (emb.cos() * self.scaling).bfloat16(), (emb.sin() * self.scaling).bfloat16()
+        return emb.cos() * self.scaling, emb.sin() * self.scaling
 
 
 def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """``x * cos + rotate_half(x) * sin`` for ``x [N, heads, D]``."""
+    """``x * cos + rotate_half(x) * sin`` for ``x [N, heads, D]`` (torch reference)."""
     half = x.shape[-1] // 2
     x1, x2 = x[..., :half], x[..., half:]
     rot = torch.cat((-x2, x1), dim=-1)
@@ -124,9 +130,6 @@ class Layer:
         self.selector = sel
 
 
-AttentionFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, "Layer"], torch.Tensor]
-
-
 class PrefillModel:
     """Random-init MiniCPM-shaped model: ``prefill(token ids) -> last-token logits``."""
 
@@ -148,32 +151,28 @@ class PrefillModel:
 
     # -- pieces ----------------------------------------------------------------------
 
-    def qkv(self, layer: Layer, h: torch.Tensor, cos, sin):
+    def qkv(self, layer: Layer, h: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor):
+        """RMSNorm -> fused QKV GEMM -> LongRoPE (fused kernel): contiguous q, k, v."""
         s = self.shape
-        x = rms_norm(h, layer.norm_in, s.rms_eps)
+        x = hk.rms_norm(h, layer.norm_in, s.rms_eps)
         qkv = x @ layer.w_qkv.t()
-        n = h.shape[0]
-        q = qkv[:, : s.num_heads * s.head_dim].view(n, s.num_heads, s.head_dim)
-        k = qkv[:, s.num_heads * s.head_dim:(s.num_heads + s.num_kv_heads) * s.head_dim]
-        v = qkv[:, (s.num_heads + s.num_kv_heads) * s.head_dim:]
-        k = k.reshape(n, s.num_kv_heads, s.head_dim)
-        v = v.reshape(n, s.num_kv_heads, s.head_dim).contiguous()
-        return apply_rope(q, cos, sin), apply_rope(k, cos, sin), v
+        del x
+        return hk.rope_split(qkv, positions, freqs, self.rope.scaling, s.num_heads,
+                             s.num_kv_heads, s.head_dim)
 
     def mlp_residual(self, layer: Layer, h: torch.Tensor) -> torch.Tensor:
+        """``h += scale * down(silu(gate(x)) * up(x))``, chunked over tokens."""
         s = self.shape
-        inter = s.intermediate_size
         for start in range(0, h.shape[0], self.mlp_chunk):
             hc = h[start:start + self.mlp_chunk]
-            x = rms_norm(hc, layer.norm_post, s.rms_eps)
-            gu = x @ layer.w_gate_up.t()
-            act = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
-            hc.add_(act @ layer.w_down.t(), alpha=self.residual_scale)
+            x = hk.rms_norm(hc, layer.norm_post, s.rms_eps)
+            act = hk.silu_mul(x @ layer.w_gate_up.t())
+            hc.addmm_(act, layer.w_down.t(), alpha=self.residual_scale)
         return h
 
     def logits(self, h_last: torch.Tensor) -> torch.Tensor:
         s = self.shape
-        x = rms_norm(h_last, self.norm_final, s.rms_eps)
+        x = hk.rms_norm(h_last, self.norm_final, s.rms_eps)
         return (x @ self.lm_head.t()).float() / (s.hidden_size / s.dim_model_base)
 
     # -- single-device prefill ---------------------------------------------------------
@@ -190,18 +189,18 @@ class PrefillModel:
         s = self.shape
         lengths = [int(n) for n in lengths]
         positions = torch.cat([torch.arange(n, device=self.device) for n in lengths])
-        cos, sin = self.rope.tables(positions, max(lengths))
+        freqs = self.rope.frequencies(max(lengths))
         h = self.embed[input_ids] * s.scale_emb
         max_len = max(lengths)
         for layer in self.layers:
-            q, k, v = self.qkv(layer, h, cos, sin)
+            q, k, v = self.qkv(layer, h, positions, freqs)
             attn, idx = prefill_layer_attention(q, k, v, cu_seqlens, max_len, layer.selector,
                                                 s.sparse, lengths=lengths, return_topk=True,
                                                 timers=timers)
             if key_counts is not None:
                 key_counts.append(count_attended_keys(idx, lengths, s.sparse.block_size))
             del q, k, v, idx
-            h.add_(attn.view(h.shape[0], -1) @ layer.w_o.t(), alpha=self.residual_scale)
+            h.addmm_(attn.view(h.shape[0], -1), layer.w_o.t(), alpha=self.residual_scale)
             del attn
             self.mlp_residual(layer, h)
         last = cu_seqlens[1:].long() - 1

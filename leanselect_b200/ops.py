@@ -269,13 +269,20 @@ def select_pages(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
     if take == 0 or total_q == 0:
         return idx
     cu_q, cu_c = _i32(cu_seqlens_q), _i32(cu_seqlens_c)
+    ws = _workspace(dev, total_q, G, int(max_seqlen_q))
     _native.call("ls_select_pages", qb.data_ptr(), weights.wq_t.data_ptr(),
                  _ptr(ks) if total_c else None, cu_q.data_ptr(), cu_c.data_ptr(),
                  cu_q.numel() - 1, int(max_seqlen_q), total_q, total_c, weights.num_heads, G,
                  weights.head_dim, weights.width, int(take), int(init_blocks), int(local_blocks),
-                 block_size, kernel_stride, idx.data_ptr(), status_word(dev).data_ptr(),
-                 _stream(dev))
+                 block_size, kernel_stride, idx.data_ptr(), ws.data_ptr(), ws.numel(),
+                 status_word(dev).data_ptr(), _stream(dev))
     return idx
+
+
+def _workspace(dev: torch.device, rows: int, groups: int, seq_len: int) -> torch.Tensor:
+    """Scratch for the selection kernels, from PyTorch's caching allocator."""
+    nbytes = _native.load().ls_select_pages_workspace_bytes(rows, groups, seq_len)
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=dev)
 
 
 def select_pages_chunk(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor, *,
@@ -297,11 +304,12 @@ def select_pages_chunk(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor
     idx = torch.empty(G, n, take, dtype=torch.int32, device=dev)
     if take == 0 or n == 0:
         return idx
+    ws = _workspace(dev, n, G, int(seq_len))
     _native.call("ls_select_pages_chunk", qb.data_ptr(), weights.wq_t.data_ptr(),
                  _ptr(ks) if total_c else None, n, int(q_position), int(seq_len), total_c,
                  weights.num_heads, G, weights.head_dim, weights.width, int(take),
                  int(init_blocks), int(local_blocks), block_size, kernel_stride, idx.data_ptr(),
-                 status_word(dev).data_ptr(), _stream(dev))
+                 ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(), _stream(dev))
     return idx
 
 

@@ -94,7 +94,7 @@ class SequenceParallelRunner:
         c = chunks[0][1]
         local_ids = torch.cat([ids[a:a + c] for a, _ in chunks])
         positions = local_positions(n, self.world, self.rank, device=self.device)
-        cos, sin = m.rope.tables(positions, n)
+        freqs = m.rope.frequencies(n)
         h = m.embed[local_ids] * s.scale_emb
         cu_full = self._cu(0, n)
         cfg = s.sparse
@@ -109,7 +109,7 @@ class SequenceParallelRunner:
             return ev
 
         for layer in m.layers:
-            q, k, v = m.qkv(layer, h, cos, sin)
+            q, k, v = m.qkv(layer, h, positions, freqs)
             kv = torch.stack((k.reshape(2 * c, -1), v.reshape(2 * c, -1)), dim=1)
             full = gather_sequence(kv, n, self.group)           # [n, 2, G*D]
             k_full = full[:, 0].reshape(n, s.num_kv_heads, s.head_dim).contiguous()
@@ -143,7 +143,7 @@ class SequenceParallelRunner:
                                                  positions=positions[i * c:(i + 1) * c])
                 key_counts.append(total)
             del q, k_full, v_full, kc, ks, idxs
-            h.add_(attn.view(h.shape[0], -1) @ layer.w_o.t(), alpha=m.residual_scale)
+            h.addmm_(attn.view(h.shape[0], -1), layer.w_o.t(), alpha=m.residual_scale)
             del attn
             m.mlp_residual(layer, h)
         if self.rank == 0:

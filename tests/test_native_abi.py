@@ -14,12 +14,12 @@ import leanselect_b200 as lsb
 from leanselect_b200 import _native
 
 ROOT = Path(__file__).resolve().parents[1]
-HEADER = ROOT / "include" / "leanselect_b200.h"
+HEADERS = sorted((ROOT / "include").glob("*.h"))
 
 
 def declared_functions():
-    text = HEADER.read_text()
-    return sorted(set(re.findall(r"^(?:const char\*|int)\s+(ls_\w+)\(", text, flags=re.M)))
+    text = "\n".join(h.read_text() for h in HEADERS)
+    return sorted(set(re.findall(r"^(?:const char\*|int|size_t)\s+(ls_\w+)\(", text, flags=re.M)))
 
 
 def test_library_exports_every_declared_symbol():
@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     assert len(names) >= 11
     for name in names:
         assert hasattr(lib, name), name
-    assert set(_native.SIGNATURES) | set(_native.STRING_FUNCS) == set(names)
+    assert set(_native.SIGNATURES) | set(_native.STRING_FUNCS) | set(_native.SIZE_FUNCS) == set(names)
 
 
 def test_version_and_status_strings():
@@ -51,16 +51,28 @@ def test_unsupported_geometry_is_reported():
     lib = _native.load()
     fake = ctypes.c_void_p(1 << 20)  # never dereferenced: validation fails first
     rc = lib.ls_select_pages(fake, fake, fake, fake, fake, 1, 64, 64, 3, 32, 2, 64, 128, 5, 1, 2,
-                             64, 16, fake, None, None)
+                             64, 16, fake, fake, 1 << 20, None, None)
     assert rc == _native.LS_ERR_UNSUPPORTED
     rc = lib.ls_select_pages(fake, fake, fake, fake, fake, 1, 64, 64, 3, 32, 2, 128, 128, 129, 1,
-                             2, 64, 16, fake, None, None)
+                             2, 64, 16, fake, fake, 1 << 20, None, None)
     assert rc == _native.LS_ERR_UNSUPPORTED  # take > LS_MAX_TOPK
     rc = lib.ls_sparse_attn(fake, fake, fake, fake, fake, 1, 64, 64, 64, 64, 24, 2, 128, fake, 4,
                             64, 0.0, 1, fake, None, None, None)
     assert rc == _native.LS_ERR_UNSUPPORTED  # 12 heads per group
     rc = lib.ls_compress_keys(fake, fake, 1, 64, 2, 128, 48, 16, fake, fake, 3, None, None)
     assert rc == _native.LS_ERR_UNSUPPORTED  # kernel_size/stride = 3
+
+
+def test_workspace_size_and_check():
+    lib = _native.load()
+    # 2 groups x 1000 rows x round8(ceil(1000/64) = 16) pages x 4 bytes
+    assert lib.ls_select_pages_workspace_bytes(1000, 2, 1000) == 2 * 1000 * 16 * 4
+    assert lib.ls_select_pages_workspace_bytes(1000, 2, 1100) == 2 * 1000 * 24 * 4
+    fake = ctypes.c_void_p(1 << 20)
+    rc = lib.ls_select_pages(fake, fake, fake, fake, fake, 1, 1000, 1000, 61, 32, 2, 128, 128, 35,
+                             1, 2, 64, 16, fake, fake, 100, None, None)
+    assert rc == _native.LS_ERR_INVALID_ARGUMENT
+    assert b"workspace" in lib.ls_last_error()
 
 
 def test_misaligned_pointer_is_reported():
