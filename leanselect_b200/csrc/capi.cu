@@ -411,6 +411,7 @@ int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
   a.out = out;
   a.lse = lse;
   a.status = status;
+  a.order = 1;  // group-major: resident CTAs share one group's K/V in L2
   const cudaError_t err = launch_sparse_attn(a, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? LS_OK : cuda_fail(err, "sparse_attn launch");
 }

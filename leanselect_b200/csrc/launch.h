@@ -78,6 +78,7 @@ struct AttnArgs {
   uint16_t* out;
   float* lse;
   int32_t* status;
+  int order;           // CTA order: 0 token-major (groups interleaved), 1 group-major
 };
 
 cudaError_t launch_sparse_attn(const AttnArgs& args, cudaStream_t stream);

@@ -119,10 +119,10 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Group-major order: CTAs resident together work on one KV group, so the
-  // K/V they gather (one group, 67 MB at 128K tokens) stays in L2.
-  const int64_t t = blockIdx.x % args.total_q;
-  const int g = static_cast<int>(blockIdx.x / args.total_q);
+  const bool group_major = args.order == 1;
+  const int64_t t = group_major ? blockIdx.x % args.total_q : blockIdx.x / args.num_groups;
+  const int g = group_major ? static_cast<int>(blockIdx.x / args.total_q)
+                            : static_cast<int>(blockIdx.x % args.num_groups);
   const int b = find_sequence(args.cu_q, args.batch, t);
   const int64_t q_start = __ldg(args.cu_q + b);
   const int64_t k_start = __ldg(args.cu_k + b);

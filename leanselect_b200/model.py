@@ -58,7 +58,8 @@ class MiniCPMShape:
     def small_24l(cls, **kw) -> "MiniCPMShape":
         """24 layers, hidden 2048, 16/2 heads, head_dim 128."""
         base = dict(hidden_size=2048, intermediate_size=8192, num_layers=24, num_heads=16,
-                    num_kv_heads=2, max_position=32768, original_max_position=32768)
+                    num_kv_heads=2, max_position=32768, original_max_position=32768,
+                    router_heads=4, router_dim=32)
         base.update(kw)
         return cls(**base)
 
@@ -125,6 +126,15 @@ class Layer:
                                  router_heads=shape.router_heads, router_dim=shape.router_dim)
         sel = sel.to(device)
         with torch.no_grad():
+            # Every selector tensor comes from the model's seeded generator, so
+            # two models built with one seed (e.g. on different ranks) agree.
+            width = shape.router_heads * shape.router_dim
+            raw = torch.randn(max(D, width), min(D, width), device=device, generator=gen)
+            frame = torch.linalg.qr(raw.float().cpu(), mode="reduced").Q
+            frame = frame if width <= D else frame.T
+            proj = (frame * D ** -0.25).reshape(D, shape.router_heads, shape.router_dim)
+            sel.q_proj.copy_(proj.permute(1, 0, 2))
+            sel.k_proj.copy_(proj.permute(1, 0, 2))
             sel.head_mix.copy_(torch.randn(H, shape.router_heads, device=device, generator=gen)
                                / math.sqrt(shape.router_heads))
         self.selector = sel

@@ -63,7 +63,7 @@ def test_silu_mul_kernel():
 def small_shape():
     return MiniCPMShape(vocab_size=1000, hidden_size=2048, intermediate_size=4096, num_layers=2,
                         num_heads=16, num_kv_heads=2, max_position=8192,
-                        original_max_position=4096)
+                        original_max_position=4096, router_heads=4, router_dim=32)
 
 
 def test_prefill_is_finite_and_deterministic():
