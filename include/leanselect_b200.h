@@ -178,6 +178,26 @@ int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
                     size_t workspace_bytes, int32_t* status, void* stream);
 
 /*
+ * ls_select_pages_noalloc -- ls_select_pages for callers that cannot
+ * allocate device memory (no counterpart in the reference, whose PyTorch
+ * code always allocates through its caching allocator).  Same arguments
+ * minus the workspace: scratch comes from a 16 MiB buffer compiled into the
+ * library (one per GPU, held until the process exits), so requests with
+ * ls_select_pages_workspace_bytes(total_q, G, max_seqlen_q) above 16 MiB
+ * (e.g. one 2-group sequence longer than ~11.5K tokens) return
+ * LS_ERR_UNSUPPORTED.  The first call on each device looks up the buffer's
+ * device address; make that first call before any stream capture.  Calls
+ * share the buffer: calls that overlap on the GPU race, so serialise them.
+ */
+int ls_select_pages_noalloc(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                            const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_c,
+                            int32_t batch, int32_t max_seqlen_q, int64_t total_q,
+                            int64_t total_c, int32_t num_heads, int32_t num_kv_heads,
+                            int32_t head_dim, int32_t width, int32_t take, int32_t init_blocks,
+                            int32_t local_blocks, int32_t block_size, int32_t kernel_stride,
+                            int32_t* topk_idx, int32_t* status, void* stream);
+
+/*
  * ls_select_pages_chunk -- ls_select_pages for a slice of ONE sequence, used
  * by the sequence-parallel prefill (no reference counterpart: the reference
  * prefill runs on one GPU).  q holds chunk_q query rows at positions

@@ -41,6 +41,8 @@ SIGNATURES = {
                        _I32, _P, _P, _P],
     "ls_select_pages": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _I32,
                         _I32, _I32, _I32, _I32, _P, _P, _SZ, _P, _P],
+    "ls_select_pages_noalloc": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32,
+                                _I32, _I32, _I32, _I32, _I32, _I32, _P, _P, _P],
     "ls_select_pages_chunk": [_P, _P, _P, _I64, _I32, _I32, _I64, _I32, _I32, _I32, _I32, _I32,
                               _I32, _I32, _I32, _I32, _P, _P, _SZ, _P, _P],
     "ls_bb_rms_norm": [_P, _P, _I64, _I32, _F32, _P, _P],

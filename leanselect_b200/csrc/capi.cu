@@ -64,7 +64,7 @@ bool make_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t rows, uint6
   return res == CUDA_SUCCESS;
 }
 
-size_t score_smem_bytes(int mode);
+int set_host_error(int code, const char* message) { return fail(code, "%s", message); }
 
 }  // namespace ls
 

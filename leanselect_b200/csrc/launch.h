@@ -83,6 +83,9 @@ struct AttnArgs {
 
 cudaError_t launch_sparse_attn(const AttnArgs& args, cudaStream_t stream);
 
+// Records `message` as the calling thread's ls_last_error() text; returns `code`.
+int set_host_error(int code, const char* message);
+
 // Builds a 2-D bf16 tensor map (row-major [rows, cols], 128B swizzle).
 // Returns false if the driver entry point is unavailable or encoding fails.
 bool make_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
