@@ -108,7 +108,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_
 }
 
 // ---------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), no multicast
+// TMA tile loads (cp.async.bulk.tensor) into this CTA's own shared memory
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
