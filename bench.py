@@ -285,8 +285,12 @@ def run_ours(args):
     achieved = flops_per_launch / (attn_ms / 1e3) / 1e12
     peak = pk["bf16_tflops_sustained"]
     # Our kernels per layer: compressed seqlens, compression, key projection,
-    # fused score/select, sparse attention.
-    launches_per_layer = 5
+    # then scoring, top-k and sparse attention once per query chunk (one chunk
+    # on a single GPU, two zig-zag chunks per rank when sequence-parallel);
+    # plus the host model's fused RMSNorm (2 + MLP chunks), RoPE and SiLU kernels.
+    chunks = 1 if world == 1 else 2
+    mlp_chunks = -(-(n // world) // 16384)
+    launches_per_layer = 3 + 3 * chunks + (1 + 2 * mlp_chunks + 1)
     line = {
         "metric": METRIC,
         "value": value,
