@@ -22,8 +22,11 @@
 // topk_kernel (select mode, a7 minicpm.py:3124-3141): one warp per (group,
 // query row) reads the row's candidate pages (visible, not forced) from the
 // workspace and finds the best T' = min(take_b, P_b) - forced by an exact
-// MSB-first radix select on order-preserving 32-bit keys (4 passes of 8
-// bits, histograms in shared memory), breaking ties toward the lower page.
+// MSB-first radix select on order-preserving 32-bit keys (8 bits per pass,
+// warp histograms in shared memory with one atomic per distinct bin; after
+// two passes the few keys left in the boundary bin are compacted into shared
+// memory and the last two bytes are resolved there), breaking ties toward
+// the lower page.
 // It writes sink pages, selected pages and local pages -- ascending -- then
 // -1 padding.
 //
@@ -368,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
 // ---------------------------------------------------------------------------
 
 constexpr int kTopkWarps = 8;
+constexpr int kListCap = 256;   // boundary candidates kept in shared memory per warp
 
 // Order-preserving map of fp32 to uint32; -inf and NaN map to 0 (never picked).
 __device__ __forceinline__ uint32_t score_key(float s) {
@@ -376,11 +380,59 @@ __device__ __forceinline__ uint32_t score_key(float s) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Adds 1 to hist[bin] for every active lane, one shared atomic per distinct bin.
+__device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool active) {
+  const uint32_t act = __ballot_sync(0xffffffffu, active);
+  if (!active) return;
+  const uint32_t peers = __match_any_sync(act, bin);
+  if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
+}
+
+// Finds, from the top, the 8-bit bin in which the `need`-th largest key lies.
+// Lane l owns bins 255-8l .. 248-8l.  Returns the bin and the count above it.
+__device__ __forceinline__ void find_bin(const uint32_t* hist, int need, int lane, int& bin,
+                                         uint32_t& above) {
+  uint32_t c[8];
+  uint32_t lane_sum = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    c[j] = hist[255 - 8 * lane - j];
+    lane_sum += c[j];
+  }
+  uint32_t incl = lane_sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const uint32_t excl = incl - lane_sum;
+  const bool here = excl < static_cast<uint32_t>(need) && incl >= static_cast<uint32_t>(need);
+  const int owner = __ffs(__ballot_sync(0xffffffffu, here)) - 1;
+  int b = 0;
+  uint32_t a = 0;
+  if (here) {
+    uint32_t cum = excl;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (cum + c[j] >= static_cast<uint32_t>(need)) {
+        b = 255 - 8 * lane - j;
+        a = cum;
+        break;
+      }
+      cum += c[j];
+    }
+  }
+  bin = __shfl_sync(0xffffffffu, b, owner);
+  above = __shfl_sync(0xffffffffu, a, owner);
+}
+
 __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_constant__ ScoreArgs args) {
   __shared__ uint32_t hist_all[kTopkWarps][256];
+  __shared__ uint32_t list_all[kTopkWarps][kListCap];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   uint32_t* hist = hist_all[warp];
+  uint32_t* list = list_all[warp];
   const int64_t rows_total = static_cast<int64_t>(args.num_groups) * args.total_q;
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * kTopkWarps + warp; r < rows_total;
        r += static_cast<int64_t>(gridDim.x) * kTopkWarps) {
@@ -418,67 +470,87 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
     }
     const int sinks_out = min(n_init, take_b);
     for (int k = lane; k < sinks_out; k += 32) out[k] = k;
+    const float* cand = scores + n_init;
 
-    // ---- threshold key by MSB-first radix select over the candidates.
-    uint32_t prefix = 0, mask = 0;
+    // ---- threshold key: the cap-th largest key, by MSB-first radix select.
+    uint32_t prefix = 0;
     int need = cap;
-    int valid_total = 0;
+    bool select_all = true;
     if (cap > 0) {
-      // Count finite candidates first: if all fit, no selection is needed.
-      for (int i = lane; i < m; i += 32) valid_total += score_key(scores[n_init + i]) != 0u;
+      // Pass 1: histogram of the top byte, counting finite candidates.
+      for (int k = lane; k < 256; k += 32) hist[k] = 0;
+      __syncwarp();
+      int valid = 0;
+      for (int base = 0; base < m; base += 32) {
+        const int i = base + lane;
+        const uint32_t key = i < m ? score_key(cand[i]) : 0u;
+        valid += key != 0u;
+        hist_add(hist, key >> 24, key != 0u);
+      }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) valid_total += __shfl_xor_sync(0xffffffffu, valid_total, o);
-    }
-    const bool select_all = valid_total <= cap;
-    if (cap > 0 && !select_all) {
-#pragma unroll 1
-      for (int pass = 0; pass < 4; ++pass) {
-        const int shift = 24 - 8 * pass;
+      for (int o = 16; o > 0; o >>= 1) valid += __shfl_xor_sync(0xffffffffu, valid, o);
+      __syncwarp();
+      select_all = valid <= cap;
+      if (!select_all) {
+        int bin;
+        uint32_t above;
+        find_bin(hist, need, lane, bin, above);
+        need -= static_cast<int>(above);
+        prefix = static_cast<uint32_t>(bin) << 24;
+        // Pass 2: second byte among keys sharing the top byte.
+        __syncwarp();
         for (int k = lane; k < 256; k += 32) hist[k] = 0;
         __syncwarp();
-        for (int i = lane; i < m; i += 32) {
-          const uint32_t key = score_key(scores[n_init + i]);
-          if (key != 0u && ((key ^ prefix) & mask) == 0) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        for (int base = 0; base < m; base += 32) {
+          const int i = base + lane;
+          const uint32_t key = i < m ? score_key(cand[i]) : 0u;
+          const bool match = key != 0u && (key >> 24) == (prefix >> 24);
+          hist_add(hist, (key >> 16) & 255u, match);
         }
         __syncwarp();
-        // Lane l owns bins 255-8l .. 248-8l (descending).
-        uint32_t c[8];
-        uint32_t lane_sum = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          c[j] = hist[255 - 8 * lane - j];
-          lane_sum += c[j];
-        }
-        uint32_t incl = lane_sum;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += t;
-        }
-        const uint32_t excl = incl - lane_sum;
-        const bool here = excl < static_cast<uint32_t>(need) && incl >= static_cast<uint32_t>(need);
-        const uint32_t owner_mask = __ballot_sync(0xffffffffu, here);
-        const int owner = __ffs(owner_mask) - 1;
-        int bin = 0;
-        uint32_t above = 0;
-        if (here) {
-          uint32_t cum = excl;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            if (cum + c[j] >= static_cast<uint32_t>(need)) {
-              bin = 255 - 8 * lane - j;
-              above = cum;
-              break;
-            }
-            cum += c[j];
-          }
-        }
-        bin = __shfl_sync(0xffffffffu, bin, owner);
-        above = __shfl_sync(0xffffffffu, above, owner);
+        find_bin(hist, need, lane, bin, above);
         need -= static_cast<int>(above);
-        prefix |= static_cast<uint32_t>(bin) << shift;
-        mask |= 0xFFu << shift;
+        prefix |= static_cast<uint32_t>(bin) << 16;
+        // Pass 3: keys sharing the top 16 bits, compacted into shared memory
+        // when they fit; the last two bytes are then resolved from there.
         __syncwarp();
+        int listed = 0;
+        for (int base = 0; base < m; base += 32) {
+          const int i = base + lane;
+          const uint32_t key = i < m ? score_key(cand[i]) : 0u;
+          const bool match = key != 0u && (key >> 16) == (prefix >> 16);
+          const uint32_t mm = __ballot_sync(0xffffffffu, match);
+          const int slot = listed + __popc(mm & ((1u << lane) - 1));
+          if (match && slot < kListCap) list[slot] = key;
+          listed += __popc(mm);
+        }
+        __syncwarp();
+        const bool in_list = listed <= kListCap;
+#pragma unroll 1
+        for (int pass = 2; pass < 4; ++pass) {
+          const int shift = 24 - 8 * pass;
+          const uint32_t pmask = 0xFFFFFFFFu << (shift + 8);
+          for (int k = lane; k < 256; k += 32) hist[k] = 0;
+          __syncwarp();
+          if (in_list) {
+            for (int base = 0; base < listed; base += 32) {
+              const int i = base + lane;
+              const uint32_t key = i < listed ? list[i] : 0u;
+              hist_add(hist, (key >> shift) & 255u, i < listed && (key & pmask) == prefix);
+            }
+          } else {
+            for (int base = 0; base < m; base += 32) {
+              const int i = base + lane;
+              const uint32_t key = i < m ? score_key(cand[i]) : 0u;
+              hist_add(hist, (key >> shift) & 255u, key != 0u && (key & pmask) == prefix);
+            }
+          }
+          __syncwarp();
+          find_bin(hist, need, lane, bin, above);
+          need -= static_cast<int>(above);
+          prefix |= static_cast<uint32_t>(bin) << shift;
+          __syncwarp();
+        }
       }
     }
     // ---- emit candidates in page order: keys above the threshold, plus the
@@ -488,7 +560,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
       int ties_seen = 0;
       for (int base = 0; base < m; base += 32) {
         const int i = base + lane;
-        const uint32_t key = i < m ? score_key(scores[n_init + i]) : 0u;
+        const uint32_t key = i < m ? score_key(cand[i]) : 0u;
         bool take;
         if (select_all) {
           take = key != 0u;
