@@ -144,7 +144,8 @@ int ls_score_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
 /*
  * ls_select_pages_workspace_bytes -- bytes of scratch ls_select_pages needs:
  * the pooled page scores of every (group, query row), fp32, rows padded to
- * 8 pages: 4 * G * total_q * round_up(ceil(max_seqlen_q / 64), 8).
+ * 8 pages, plus four fp32 statistics per row:
+ * 4 * G * total_q * (round_up(ceil(max_seqlen_q / 64), 8) + 4).
  */
 size_t ls_select_pages_workspace_bytes(int64_t total_q, int32_t num_kv_heads,
                                        int32_t max_seqlen_q);
@@ -184,7 +185,7 @@ int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
  * minus the workspace: scratch comes from a 16 MiB buffer compiled into the
  * library (one per GPU, held until the process exits), so requests with
  * ls_select_pages_workspace_bytes(total_q, G, max_seqlen_q) above 16 MiB
- * (e.g. one 2-group sequence longer than ~11.5K tokens) return
+ * (e.g. one 2-group sequence longer than about 11K tokens) return
  * LS_ERR_UNSUPPORTED.  The first call on each device looks up the buffer's
  * device address; make that first call before any stream capture.  Calls
  * share the buffer: calls that overlap on the GPU race, so serialise them.

@@ -352,3 +352,20 @@ def test_cpu_tensors_are_rejected():
     sel = lsb.LeanSelectSelector(num_heads=32, num_kv_heads=2, head_dim=128)
     with pytest.raises(RuntimeError):
         sel.project_queries(torch.zeros(4, 32, 128))
+
+
+def test_select_pages_exact_ties_pick_lowest_pages():
+    """All scores equal (zero head mix): the lowest candidate pages win, as in the oracle."""
+    lens = [3000, 1000]
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=2, seed=81, bf16=True)
+    inp.params.head_mix[:] = 0.0
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    from leanselect_b200.attention import _LayerView
+    view = _LayerView(lsb.LayerConfig(topk=20), selector_for(inp.params))
+    got = lsb.lightweight_compressed_attention(view, to_dev(inp.q), to_dev(kc),
+                                               cu_dev(inp.cu_seqlens), cu_dev(cu_c),
+                                               max(lens)).cpu().numpy()
+    want = ora.lightweight_compressed_attention(inp.q, kc, inp.cu_seqlens, cu_c, inp.params,
+                                                topk=20, policy="bf16")
+    np.testing.assert_array_equal(np.sort(got, -1), np.sort(want.topk_idx, -1))
