@@ -144,8 +144,7 @@ int ls_score_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
 /*
  * ls_select_pages_workspace_bytes -- bytes of scratch ls_select_pages needs:
  * the pooled page scores of every (group, query row), fp32, rows padded to
- * 8 pages, plus four fp32 statistics per row:
- * 4 * G * total_q * (round_up(ceil(max_seqlen_q / 64), 8) + 4).
+ * 8 pages: 4 * G * total_q * round_up(ceil(max_seqlen_q / 64), 8).
  */
 size_t ls_select_pages_workspace_bytes(int64_t total_q, int32_t num_kv_heads,
                                        int32_t max_seqlen_q);

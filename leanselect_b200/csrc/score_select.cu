@@ -21,14 +21,9 @@
 //
 // topk_kernel (select mode, a7 minicpm.py:3124-3141): one warp per (group,
 // query row) reads the row's candidate pages (visible, not forced) from the
-// workspace and finds the best T' = min(take_b, P_b) - forced, breaking ties
-// toward the lower page.  The scoring epilogue also leaves each row's count,
-// max, sum and sum of squares of candidate scores; the warp histograms the
-// scores in 256 linear bins of width sigma/32 below the max, finds the bin
-// holding the T'-th best, collects that bin's few candidates in shared memory
-// and ranks them exactly.  Degenerate rows (a zero spread, or a boundary bin
-// with more than 256 candidates) fall back to an exact MSB-first radix select
-// on order-preserving 32-bit keys.
+// workspace and finds the best T' = min(take_b, P_b) - forced by an exact
+// MSB-first radix select on order-preserving 32-bit keys (4 passes of 8
+// bits, histograms in shared memory), breaking ties toward the lower page.
 // It writes sink pages, selected pages and local pages -- ascending -- then
 // -1 padding.
 //
@@ -306,12 +301,6 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
                        (static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_pages;
       float carry = -INFINITY;  // score of the last atom of the previous tile
       const int last_atom = ti.atoms - 1;
-      // Select mode: count, max, sum and sum of squares of the row's finite
-      // candidate scores (pages n_init .. lo-1), handed to the top-k kernel.
-      const int qp_row = (ti.pos0 + ti.row0 + row) / 64;
-      const int cand_lo = min(args.init_blocks, qp_row + 1);
-      const int cand_hi = max(0, qp_row - args.local_blocks);
-      float st_cnt = 0.f, st_max = -INFINITY, st_sum = 0.f, st_sq = 0.f;
       for (int j = 0; j < ti.atom_tiles && ok; ++j) {
         const int buf = j & 1;
         ok = mbar_wait(&bars->s_full[buf], (j >> 1) & 1, status, abort_flag);
@@ -333,17 +322,6 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
           }
           carry = v[31];
           const int p0 = j * 32 + q * 8;
-          if (MODE == kModeSelect) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              if (p0 + i >= cand_lo && p0 + i < cand_hi && pg[i] > -INFINITY) {
-                st_cnt += 1.f;
-                st_max = fmaxf(st_max, pg[i]);
-                st_sum += pg[i];
-                st_sq = fmaf(pg[i], pg[i], st_sq);
-              }
-            }
-          }
           if (valid && p0 < args.max_pages) {
             if (MODE == kModeScore) {
 #pragma unroll
@@ -373,19 +351,6 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
                                            : min(args.max_pages, qp - args.local_blocks);
         for (int p = ti.atom_tiles * 32; p < end; ++p)
           out_row[p] = (p == ti.atom_tiles * 32 && p < ti.pages) ? carry : -INFINITY;
-        if (MODE == kModeSelect) {
-          const int p = ti.atom_tiles * 32;
-          if (p >= cand_lo && p < cand_hi && p < ti.pages && carry > -INFINITY) {
-            st_cnt += 1.f;
-            st_max = fmaxf(st_max, carry);
-            st_sum += carry;
-            st_sq = fmaf(carry, carry, st_sq);
-          }
-          float4* stats = reinterpret_cast<float4*>(
-              args.workspace + static_cast<int64_t>(args.num_groups) * args.total_q * args.max_pages);
-          stats[static_cast<int64_t>(ti.g) * args.total_q + q_row] =
-              make_float4(st_cnt, st_max, st_sum, st_sq);
-        }
       }
     }
   }
@@ -403,8 +368,6 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
 // ---------------------------------------------------------------------------
 
 constexpr int kTopkWarps = 8;
-constexpr int kListCap = 256;   // boundary candidates resolved in shared memory per warp
-constexpr int kBins = 256;
 
 // Order-preserving map of fp32 to uint32; -inf and NaN map to 0 (never picked).
 __device__ __forceinline__ uint32_t score_key(float s) {
@@ -413,79 +376,12 @@ __device__ __forceinline__ uint32_t score_key(float s) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Linear bin below the row maximum: 0 for the max, kBins-1 and above clamped.
-__device__ __forceinline__ int score_bin(float s, float mx, float inv_w) {
-  const float d = (mx - s) * inv_w;  // monotone non-increasing in s
-  return d < static_cast<float>(kBins - 1) ? static_cast<int>(d) : kBins - 1;
-}
-
-// Exact threshold key of the `need`-th largest candidate key by MSB-first
-// radix select (8 bits per pass).  Returns the key; `need` becomes the number
-// of candidates equal to it that are selected.
-__device__ uint32_t radix_threshold(const float* cand, int m, int& need, uint32_t* hist, int lane) {
-  uint32_t prefix = 0, mask = 0;
-#pragma unroll 1
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    for (int k = lane; k < 256; k += 32) hist[k] = 0;
-    __syncwarp();
-    for (int i = lane; i < m; i += 32) {
-      const uint32_t key = score_key(cand[i]);
-      if (key != 0u && ((key ^ prefix) & mask) == 0) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-    }
-    __syncwarp();
-    // Lane l owns bins 255-8l .. 248-8l (descending).
-    uint32_t c[8];
-    uint32_t lane_sum = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      c[j] = hist[255 - 8 * lane - j];
-      lane_sum += c[j];
-    }
-    uint32_t incl = lane_sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
-    }
-    const uint32_t excl = incl - lane_sum;
-    const bool here = excl < static_cast<uint32_t>(need) && incl >= static_cast<uint32_t>(need);
-    const int owner = __ffs(__ballot_sync(0xffffffffu, here)) - 1;
-    int bin = 0;
-    uint32_t above = 0;
-    if (here) {
-      uint32_t cum = excl;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (cum + c[j] >= static_cast<uint32_t>(need)) {
-          bin = 255 - 8 * lane - j;
-          above = cum;
-          break;
-        }
-        cum += c[j];
-      }
-    }
-    bin = __shfl_sync(0xffffffffu, bin, owner);
-    above = __shfl_sync(0xffffffffu, above, owner);
-    need -= static_cast<int>(above);
-    prefix |= static_cast<uint32_t>(bin) << shift;
-    mask |= 0xFFu << shift;
-    __syncwarp();
-  }
-  return prefix;
-}
-
 __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_constant__ ScoreArgs args) {
-  __shared__ uint32_t hist_all[kTopkWarps][kBins];
-  __shared__ float list_s_all[kTopkWarps][kListCap];
-  __shared__ int32_t list_p_all[kTopkWarps][kListCap];
+  __shared__ uint32_t hist_all[kTopkWarps][256];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   uint32_t* hist = hist_all[warp];
-  float* list_s = list_s_all[warp];
-  int32_t* list_p = list_p_all[warp];
   const int64_t rows_total = static_cast<int64_t>(args.num_groups) * args.total_q;
-  const float4* stats = reinterpret_cast<const float4*>(args.workspace + rows_total * args.max_pages);
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * kTopkWarps + warp; r < rows_total;
        r += static_cast<int64_t>(gridDim.x) * kTopkWarps) {
     const int64_t q_row = r % args.total_q;
@@ -522,142 +418,91 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
     }
     const int sinks_out = min(n_init, take_b);
     for (int k = lane; k < sinks_out; k += 32) out[k] = k;
-    const float* cand = scores + n_init;
 
-    // mode 0: take every finite candidate; 1: linear bins below the max with
-    // the boundary bin resolved exactly in shared memory; 2: radix threshold.
-    int mode = 0;
-    float mx = 0.f, inv_w = 0.f;
-    int b_star = 0, need = 0;
-    uint32_t thr_key = 0;
+    // ---- threshold key by MSB-first radix select over the candidates.
+    uint32_t prefix = 0, mask = 0;
+    int need = cap;
+    int valid_total = 0;
     if (cap > 0) {
-      const float4 st = stats[r];
-      if (static_cast<int>(st.x) > cap) {
-        mode = 2;
-        need = cap;
-        mx = st.y;
-        const float mean = st.z / st.x;
-        const float sigma = sqrtf(fmaxf(st.w / st.x - mean * mean, 0.f));
-        const float w = sigma * (1.f / 32.f);
-        if (isfinite(mx) && w > 0.f && isfinite(w)) {
-          inv_w = 1.f / w;
-          // Pass A: histogram of the top kBins-1 bins.
-          for (int k = lane; k < kBins; k += 32) hist[k] = 0;
-          __syncwarp();
-          for (int i = lane; i < m; i += 32) {
-            const float sc = cand[i];
-            if (sc > -INFINITY) {
-              const int bin = score_bin(sc, mx, inv_w);
-              if (bin < kBins - 1) atomicAdd(&hist[bin], 1u);
-            }
-          }
-          __syncwarp();
-          // Lane l owns bins 8l .. 8l+7 (highest scores first).
-          uint32_t c[8];
-          uint32_t lane_sum = 0;
+      // Count finite candidates first: if all fit, no selection is needed.
+      for (int i = lane; i < m; i += 32) valid_total += score_key(scores[n_init + i]) != 0u;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) valid_total += __shfl_xor_sync(0xffffffffu, valid_total, o);
+    }
+    const bool select_all = valid_total <= cap;
+    if (cap > 0 && !select_all) {
+#pragma unroll 1
+      for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int k = lane; k < 256; k += 32) hist[k] = 0;
+        __syncwarp();
+        for (int i = lane; i < m; i += 32) {
+          const uint32_t key = score_key(scores[n_init + i]);
+          if (key != 0u && ((key ^ prefix) & mask) == 0) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncwarp();
+        // Lane l owns bins 255-8l .. 248-8l (descending).
+        uint32_t c[8];
+        uint32_t lane_sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          c[j] = hist[255 - 8 * lane - j];
+          lane_sum += c[j];
+        }
+        uint32_t incl = lane_sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const uint32_t excl = incl - lane_sum;
+        const bool here = excl < static_cast<uint32_t>(need) && incl >= static_cast<uint32_t>(need);
+        const uint32_t owner_mask = __ballot_sync(0xffffffffu, here);
+        const int owner = __ffs(owner_mask) - 1;
+        int bin = 0;
+        uint32_t above = 0;
+        if (here) {
+          uint32_t cum = excl;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            c[j] = hist[8 * lane + j];
-            lane_sum += c[j];
-          }
-          uint32_t incl = lane_sum;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += t;
-          }
-          const uint32_t excl = incl - lane_sum;
-          const bool here = excl < static_cast<uint32_t>(cap) && incl >= static_cast<uint32_t>(cap);
-          const uint32_t owners = __ballot_sync(0xffffffffu, here);
-          if (owners != 0u) {
-            const int owner = __ffs(owners) - 1;
-            int bs = 0;
-            uint32_t above = 0;
-            if (here) {
-              uint32_t cum = excl;
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                if (cum + c[j] >= static_cast<uint32_t>(cap)) {
-                  bs = 8 * lane + j;
-                  above = cum;
-                  break;
-                }
-                cum += c[j];
-              }
+            if (cum + c[j] >= static_cast<uint32_t>(need)) {
+              bin = 255 - 8 * lane - j;
+              above = cum;
+              break;
             }
-            b_star = __shfl_sync(0xffffffffu, bs, owner);
-            above = __shfl_sync(0xffffffffu, above, owner);
-            const int listed = static_cast<int>(__shfl_sync(0xffffffffu, c[b_star & 7], b_star >> 3));
-            if (listed <= kListCap) {
-              mode = 1;
-              need = cap - static_cast<int>(above);
-              // Pass B: the boundary bin's candidates, in page order.
-              int filled = 0;
-              for (int base = 0; base < m; base += 32) {
-                const int i = base + lane;
-                const float sc = i < m ? cand[i] : -INFINITY;
-                const bool inb = sc > -INFINITY && score_bin(sc, mx, inv_w) == b_star;
-                const uint32_t bm = __ballot_sync(0xffffffffu, inb);
-                if (inb) {
-                  const int slot = filled + __popc(bm & ((1u << lane) - 1));
-                  list_s[slot] = sc;
-                  list_p[slot] = i;
-                }
-                filled += __popc(bm);
-              }
-              __syncwarp();
-              // Rank each boundary candidate (higher score, then lower page, first);
-              // keep the best `need`: their page is kept, the others marked -1.
-              for (int e = lane; e < listed; e += 32) {
-                const float se = list_s[e];
-                const int pe = list_p[e];
-                int rank = 0;
-                for (int o = 0; o < listed; ++o) {
-                  const float so = list_s[o];
-                  rank += (so > se) || (so == se && list_p[o] < pe);
-                }
-                if (rank >= need) list_p[e] = -1;
-              }
-              __syncwarp();
-            }
+            cum += c[j];
           }
         }
-        if (mode == 2) {
-          need = cap;
-          thr_key = radix_threshold(cand, m, need, hist, lane);
-        }
+        bin = __shfl_sync(0xffffffffu, bin, owner);
+        above = __shfl_sync(0xffffffffu, above, owner);
+        need -= static_cast<int>(above);
+        prefix |= static_cast<uint32_t>(bin) << shift;
+        mask |= 0xFFu << shift;
+        __syncwarp();
       }
     }
-    // ---- emit candidates in page order.
+    // ---- emit candidates in page order: keys above the threshold, plus the
+    // first `need` keys equal to it (lower pages first).
     int k_out = sinks_out;
     if (cap > 0) {
-      int ties_seen = 0, boundary_seen = 0;
+      int ties_seen = 0;
       for (int base = 0; base < m; base += 32) {
         const int i = base + lane;
-        const float sc = i < m ? cand[i] : -INFINITY;
+        const uint32_t key = i < m ? score_key(scores[n_init + i]) : 0u;
         bool take;
-        if (mode == 0) {
-          take = sc > -INFINITY;
-        } else if (mode == 1) {
-          const int bin = sc > -INFINITY ? score_bin(sc, mx, inv_w) : kBins;
-          const bool inb = bin == b_star;
-          const uint32_t bm = __ballot_sync(0xffffffffu, inb);
-          const int slot = boundary_seen + __popc(bm & ((1u << lane) - 1));
-          take = bin < b_star || (inb && list_p[slot] >= 0);
-          boundary_seen += __popc(bm);
+        if (select_all) {
+          take = key != 0u;
         } else {
-          const uint32_t key = score_key(sc);
-          const bool tie = key == thr_key;
+          const bool tie = key == prefix;
           const uint32_t tie_mask = __ballot_sync(0xffffffffu, tie);
           const int tie_rank = ties_seen + __popc(tie_mask & ((1u << lane) - 1));
-          take = key > thr_key || (tie && tie_rank < need);
+          take = key > prefix || (tie && tie_rank < need);
           ties_seen += __popc(tie_mask);
         }
         const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
         if (take) out[k_out + __popc(take_mask & ((1u << lane) - 1))] = n_init + i;
         k_out += __popc(take_mask);
       }
-      __syncwarp();
     }
     // Local pages (those that are not sinks), then padding.
     const int local_out = max(0, min(n_local, take_b - k_out));
@@ -670,8 +515,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
 }  // namespace
 
 size_t select_workspace_floats(int64_t rows, int max_pages) {
-  // Pooled page scores (rows padded to 8 pages) plus 4 statistics per row.
-  return static_cast<size_t>(rows) * static_cast<size_t>(((max_pages + 7) & ~7) + 4);
+  return static_cast<size_t>(rows) * static_cast<size_t>((max_pages + 7) & ~7);
 }
 
 cudaError_t launch_score(int mode, const ScoreArgs& args_in, cudaStream_t stream) {
