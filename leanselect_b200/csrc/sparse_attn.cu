@@ -29,6 +29,7 @@ constexpr int kStageBytes = 4 * kBoxBytes;     // K half0, K half1, V half0, V h
 constexpr int kThreads = 160;
 constexpr int kMaxT = LS_MAX_TOPK;
 constexpr int32_t kSentinel = 0x7FFFFFFF;
+constexpr float kRescaleSlack = 8.f;  // log2 units: exponentials stay below 256
 
 struct AttnSmem {
   uint64_t full[kStages];
@@ -237,22 +238,33 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
     ok = mbar_wait(&sm->full[s], (i / kStages) & 1, args.status, abort_flag);
     if (!ok) break;
     const uint32_t st = smem_u32(stages + s * kStageBytes);
-    // ---- S = Q K^T for keys key_base .. key_base+15 of this page.
-    float sc[2][4];
+    // ---- S = Q K^T for keys key_base .. key_base+15 of this page.  The
+    // head dimension is split over two accumulator sets (dims 0-63, 64-127)
+    // so four independent MMA chains are in flight.
+    float sc[2][4], sh[2][4];
 #pragma unroll
-    for (int n = 0; n < 2; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+    for (int n = 0; n < 2; ++n) {
+      sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+      sh[n][0] = sh[n][1] = sh[n][2] = sh[n][3] = 0.f;
+    }
     {
       const int mat = lane >> 3, r8 = lane & 7;
       const int key = key_base + (mat >> 1) * 8 + r8;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const int dim0 = 16 * kk + (mat & 1) * 8;
-        const uint32_t addr = st + (dim0 >> 6) * kBoxBytes + sw128(key, (dim0 & 63) >> 3);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(addr, b0, b1, b2, b3);
+      for (int kk = 0; kk < 4; ++kk) {
+        const int chunk = 2 * kk + (mat & 1);  // 16-byte chunk inside each 64-dim box
+        uint32_t b0, b1, b2, b3, c0, c1, c2, c3;
+        ldsm_x4(st + sw128(key, chunk), b0, b1, b2, b3);
+        ldsm_x4(st + kBoxBytes + sw128(key, chunk), c0, c1, c2, c3);
         mma_bf16_16816(sc[0], qa[kk], b0, b1);
         mma_bf16_16816(sc[1], qa[kk], b2, b3);
+        mma_bf16_16816(sh[0], qa[kk + 4], c0, c1);
+        mma_bf16_16816(sh[1], qa[kk + 4], c2, c3);
       }
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[n][e] += sh[n][e];
     }
     // ---- causal / length mask (only pages that reach past t_lim)
     const int page_key0 = sm->pages[i] * 64 + key_base;
@@ -265,19 +277,33 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
           if (key > t_lim) sc[n][e] = -INFINITY;
         }
     }
-    // ---- online softmax (log2 domain)
+    // ---- online softmax (log2 domain) with a lazily raised reference max:
+    // m0/m1 only move when a score exceeds them by more than kRescaleSlack,
+    // so exponentials stay below 2^kRescaleSlack and the O rescale is rare.
     float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1])) * sl2;
     float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3])) * sl2;
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
-    const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
-    const float a0 = ex2(m0 - mu0), a1 = ex2(m1 - mu1);
-    m0 = mn0;
-    m1 = mn1;
+    const bool grow0 = mx0 > m0 + kRescaleSlack, grow1 = mx1 > m1 + kRescaleSlack;
+    if (__any_sync(0xffffffffu, grow0 || grow1)) {
+      const float a0 = grow0 ? ex2(m0 - mx0) : 1.f;
+      const float a1 = grow1 ? ex2(m1 - mx1) : 1.f;
+      if (grow0) m0 = mx0;
+      if (grow1) m1 = mx1;
+      l0 *= a0;
+      l1 *= a1;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[j][0] *= a0;
+        o[j][1] *= a0;
+        o[j][2] *= a1;
+        o[j][3] *= a1;
+      }
+    }
+    const float mu0 = m0 == -INFINITY ? 0.f : m0;
+    const float mu1 = m1 == -INFINITY ? 0.f : m1;
     float p[2][4];
 #pragma unroll
     for (int n = 0; n < 2; ++n) {
@@ -286,15 +312,8 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
       p[n][2] = ex2(fmaf(sc[n][2], sl2, -mu1));
       p[n][3] = ex2(fmaf(sc[n][3], sl2, -mu1));
     }
-    l0 = l0 * a0 + (p[0][0] + p[0][1] + p[1][0] + p[1][1]);
-    l1 = l1 * a1 + (p[0][2] + p[0][3] + p[1][2] + p[1][3]);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      o[j][0] *= a0;
-      o[j][1] *= a0;
-      o[j][2] *= a1;
-      o[j][3] *= a1;
-    }
+    l0 += (p[0][0] + p[0][1]) + (p[1][0] + p[1][1]);
+    l1 += (p[0][2] + p[0][3]) + (p[1][2] + p[1][3]);
     uint32_t pa[4];
     pa[0] = pack_bf16x2(p[0][0], p[0][1]);
     pa[1] = pack_bf16x2(p[0][2], p[0][3]);
