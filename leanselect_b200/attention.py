@@ -13,6 +13,7 @@
 from __future__ import annotations
 
 from dataclasses import dataclass
+from typing import Callable
 
 import torch
 from torch import nn
@@ -136,6 +137,18 @@ class LayerConfig:
     init_blocks: int = 1
     local_blocks: int = 2
     selection_method: str = "leanselect"
+    # Optional per-sequence budget: maps a sequence length to its total page
+    # count T (e.g. min(64, pages // 10) + sink + local).
+    # The reference takes one T per packed call (minicpm.py:3104), so such a
+    # batch is selected sequence by sequence and padded to the largest T.
+    per_sequence_topk: Callable[[int], int] | None = None
+
+
+def config4_budget(seq_len: int, block_size: int = 64, init_blocks: int = 1,
+                   local_blocks: int = 2) -> int:
+    """BASELINE config 4 budget: min(64, floor(0.1 * pages)) + sink + local pages."""
+    pages = (int(seq_len) + block_size - 1) // block_size
+    return min(64, pages // 10) + init_blocks + local_blocks
 
 
 class _LayerView:
@@ -172,6 +185,29 @@ def count_attended_keys(topk_idx: torch.Tensor, lengths, block_size: int = 64,
     return int((visible * (topk_idx >= 0)).sum().item())
 
 
+def _select_per_sequence(q: torch.Tensor, kc: torch.Tensor, lens, selector: LeanSelectSelector,
+                         cfg: LayerConfig) -> torch.Tensor:
+    """Selection with a per-sequence budget: one call per sequence, padded with -1."""
+    budgets = [int(cfg.per_sequence_topk(n)) for n in lens]
+    takes = [min(t, (n + cfg.block_size - 1) // cfg.block_size) for t, n in zip(budgets, lens)]
+    idx = torch.full((selector.num_kv_heads, q.shape[0], max(takes, default=0)), -1,
+                     dtype=torch.int32, device=q.device)
+    q0 = c0 = 0
+    for n, t in zip(lens, budgets):
+        a = ops.atom_count(n, cfg.kernel_size, cfg.kernel_stride)
+        if n > 0:
+            view = _LayerView(cfg, selector)
+            view.topk = t
+            cu_q = torch.tensor([0, n], dtype=torch.int32, device=q.device)
+            cu_c = torch.tensor([0, a], dtype=torch.int32, device=q.device)
+            part = lightweight_compressed_attention(view, q[q0:q0 + n], kc[c0:c0 + a], cu_q,
+                                                    cu_c, n, q_lengths=[n])
+            idx[:, q0:q0 + n, :part.shape[2]] = part
+        q0 += n
+        c0 += a
+    return idx
+
+
 def prefill_layer_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                             cu_seqlens: torch.Tensor, max_seqlen: int,
                             selector: LeanSelectSelector, cfg: LayerConfig, *, lengths=None,
@@ -196,9 +232,14 @@ def prefill_layer_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     kc, cu_c = ops.compress_keys(k, cu_seqlens, kernel_size=cfg.kernel_size,
                                  kernel_stride=cfg.kernel_stride, lengths=lens)
     e1 = mark()
-    view = _LayerView(cfg, selector)
-    idx = lightweight_compressed_attention(view, q, kc, cu_seqlens, cu_c, max_seqlen,
-                                           q_lengths=lens)
+    if cfg.per_sequence_topk is None or len(lens) == 1:
+        view = _LayerView(cfg, selector)
+        if cfg.per_sequence_topk is not None:
+            view.topk = int(cfg.per_sequence_topk(lens[0]))
+        idx = lightweight_compressed_attention(view, q, kc, cu_seqlens, cu_c, max_seqlen,
+                                               q_lengths=lens)
+    else:
+        idx = _select_per_sequence(q, kc, lens, selector, cfg)
     e2 = mark()
     out = ops.sparse_attn(q, k, v, cu_seqlens, cu_seqlens, max_seqlen, max_seqlen, idx,
                           causal=True)

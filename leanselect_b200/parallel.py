@@ -62,6 +62,53 @@ def gather_sequence(local: torch.Tensor, seq_len: int, group=None) -> torch.Tens
                       second.reshape((-1,) + tuple(local.shape[1:]))), dim=0)
 
 
+def lpt_shards(lengths: Sequence[int], world: int) -> list[list[int]]:
+    """Longest-processing-time-first assignment of sequences to ranks.
+
+    Returns, per rank, the indices of its sequences (in input order).  Work is
+    taken as proportional to length (the dense layers are token-linear and the
+    page budget caps the attention per token).
+    """
+    loads = [0] * world
+    shards: list[list[int]] = [[] for _ in range(world)]
+    for i in sorted(range(len(lengths)), key=lambda j: (-int(lengths[j]), j)):
+        r = min(range(world), key=lambda k: (loads[k], k))
+        shards[r].append(i)
+        loads[r] += int(lengths[i])
+    return [sorted(s) for s in shards]
+
+
+class DataParallelRunner:
+    """Batched prefill: sequences sharded over ranks, no collectives.
+
+    Every rank holds the whole model (same seed), takes its LPT shard of the
+    batch, and prefills it as one packed varlen batch; ranks never exchange
+    data.  ``prefill_device`` returns this rank's ``(sequence indices, logits)``.
+    """
+
+    def __init__(self, shape: MiniCPMShape, device: torch.device | str, seed: int = 0,
+                 group=None):
+        self.device = torch.device(device)
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.model = PrefillModel(shape, self.device, seed=seed)
+
+    def prefill_device(self, ids: torch.Tensor, lengths: Sequence[int]):
+        lengths = [int(n) for n in lengths]
+        mine = lpt_shards(lengths, self.world)[self.rank]
+        if not mine:
+            return mine, None
+        offsets = [0]
+        for n in lengths:
+            offsets.append(offsets[-1] + n)
+        local_ids = torch.cat([ids[offsets[i]:offsets[i + 1]] for i in mine])
+        local_lens = [lengths[i] for i in mine]
+        cu = torch.zeros(len(mine) + 1, dtype=torch.int32)
+        cu[1:] = torch.tensor(local_lens).cumsum(0)
+        logits = self.model.prefill(local_ids, cu.to(self.device), local_lens)
+        return mine, logits
+
+
 class SequenceParallelRunner:
     """One sequence prefilled by all ranks of the default process group."""
 

@@ -369,3 +369,31 @@ def test_select_pages_exact_ties_pick_lowest_pages():
     want = ora.lightweight_compressed_attention(inp.q, kc, inp.cu_seqlens, cu_c, inp.params,
                                                 topk=20, policy="bf16")
     np.testing.assert_array_equal(np.sort(got, -1), np.sort(want.topk_idx, -1))
+
+
+def test_per_sequence_budgets_match_oracle():
+    """BASELINE config-4 style budgets: each sequence selected with its own T."""
+    from leanselect_b200.attention import config4_budget
+
+    lens = [1300, 2700, 640]
+    inp = ora.synthetic_layer(lens, num_heads=16, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=3, seed=91, bf16=True)
+    cfg = lsb.LayerConfig(per_sequence_topk=config4_budget)
+    cu = cu_dev(inp.cu_seqlens)
+    out, idx = lsb.prefill_layer_attention(to_dev(inp.q), to_dev(inp.k), to_dev(inp.v), cu,
+                                           max(lens), selector_for(inp.params), cfg,
+                                           return_topk=True)
+    idx = idx.cpu().numpy()
+    assert idx.shape[2] == max(min(config4_budget(n), (n + 63) // 64) for n in lens)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    for b, n in enumerate(lens):
+        q0, c0, c1 = inp.cu_seqlens[b], cu_c[b], cu_c[b + 1]
+        want = ora.lightweight_compressed_attention(
+            inp.q[q0:q0 + n], kc[c0:c1], np.array([0, n]), np.array([0, c1 - c0]), inp.params,
+            topk=config4_budget(n), policy="bf16")
+        got = idx[:, q0:q0 + n, :want.topk_idx.shape[2]]
+        assert np.all(idx[:, q0:q0 + n, want.topk_idx.shape[2]:] == -1)
+        bad = ora.selection_mismatches(got, want, rel_tol=1e-3)
+        assert not bad, bad[:3]
+    ref, _ = ora.sparse_attention(inp.q, inp.k, inp.v, inp.cu_seqlens, inp.cu_seqlens, idx)
+    _attn_check(out, None, ref, None)

@@ -71,3 +71,25 @@ def test_zigzag_rejects_unaligned_lengths():
         zigzag_chunks(1000, 2, 0)
     with pytest.raises(ValueError):
         zigzag_chunks(1024, 2, 2)
+
+
+def test_lpt_shards_cover_every_sequence_once_and_balance():
+    from leanselect_b200.parallel import lpt_shards
+
+    import numpy as np
+    rng = np.random.default_rng(0)
+    lengths = rng.integers(8192, 32769, 64).tolist()
+    shards = lpt_shards(lengths, 8)
+    flat = sorted(i for s in shards for i in s)
+    assert flat == list(range(64))
+    loads = [sum(lengths[i] for i in s) for s in shards]
+    assert max(loads) - min(loads) <= max(lengths)
+    assert max(loads) / (sum(lengths) / 8) < 1.05
+
+
+def test_config4_budget_rule():
+    from leanselect_b200.attention import config4_budget
+
+    assert config4_budget(8192) == 12 + 3          # 128 pages -> 12
+    assert config4_budget(32768) == 51 + 3         # 512 pages -> 51
+    assert config4_budget(131072) == 64 + 3        # capped at 64
