@@ -142,6 +142,20 @@ int ls_score_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
                    int32_t kernel_stride, float* page_scores, int32_t* status, void* stream);
 
 /*
+ * ls_atom_scores -- replaces NOSA's LlamaAttention._leanselect_atom_scores
+ * (leanselect/models/nosa.py:1822-1853): raw LeanSelect atom scores
+ * Qs[t]·Ks[a] for every (group, query row, atom of its sequence), no causal
+ * mask, as bf16 [G, total_q, max_atoms] (max_atoms = the batch's largest atom
+ * count; entries past a sequence's atoms are -inf), fed to NOSA's
+ * compressed_attention as precomputed scores.  Requires D == 128, F == 128.
+ */
+int ls_atom_scores(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                   const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_c, int32_t batch,
+                   int32_t max_seqlen_q, int64_t total_q, int64_t total_c, int32_t num_heads,
+                   int32_t num_kv_heads, int32_t head_dim, int32_t width, int32_t max_atoms,
+                   uint16_t* atom_scores, int32_t* status, void* stream);
+
+/*
  * ls_select_pages_workspace_bytes -- bytes of scratch ls_select_pages needs:
  * the pooled page scores of every (group, query row), fp32, rows padded to
  * 8 pages: 4 * G * total_q * round_up(ceil(max_seqlen_q / 64), 8).

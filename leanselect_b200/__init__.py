@@ -8,11 +8,13 @@ causal attention over the selected pages.  Hand-written CUDA behind a C ABI
 from . import ops
 from ._native import LeanSelectError, LS_MAX_TOPK, version
 from .attention import (CompressK, LayerConfig, infllmv2_attn_varlen_func,
-                        lightweight_compressed_attention, prefill_layer_attention)
+                        lightweight_compressed_attention, nosa_atom_scores,
+                        prefill_layer_attention)
 from .selector import LeanSelectSelector
 
 __all__ = [
     "ops", "LeanSelectError", "LS_MAX_TOPK", "version", "CompressK", "LayerConfig",
-    "infllmv2_attn_varlen_func", "lightweight_compressed_attention", "prefill_layer_attention",
+    "infllmv2_attn_varlen_func", "lightweight_compressed_attention", "nosa_atom_scores",
+    "prefill_layer_attention",
     "LeanSelectSelector",
 ]

@@ -39,6 +39,8 @@ SIGNATURES = {
     "ls_project_queries": [_P, _I64, _I32, _I32, _I32, _P, _I32, _P, _P, _P],
     "ls_score_pages": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _I32,
                        _I32, _P, _P, _P],
+    "ls_atom_scores": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _I32,
+                       _P, _P, _P],
     "ls_select_pages": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _I32,
                         _I32, _I32, _I32, _I32, _P, _P, _SZ, _P, _P],
     "ls_select_pages_noalloc": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32,

@@ -84,6 +84,28 @@ def lightweight_compressed_attention(module, q_unpad: torch.Tensor, k_compressed
                             kernel_stride=int(module.kernel_stride))
 
 
+def nosa_atom_scores(module, query_layer: torch.Tensor, compressed_k: torch.Tensor,
+                     cu_seqlens_q: torch.Tensor, compressed_cu_seqlens: torch.Tensor,
+                     q_lengths=None, c_lengths=None) -> torch.Tensor:
+    """NOSA's ``LlamaAttention._leanselect_atom_scores`` (nosa.py:1822-1853).
+
+    ``[G, total_q, max_atoms]`` raw LeanSelect atom scores in the query dtype,
+    ``-inf`` past each sequence's atoms, for NOSA's ``compressed_attention``
+    (``precomputed_qk_score``).  Computed by the same tcgen05 scoring kernel
+    as the MiniCPM path.
+    """
+    selector = _as_selector(module)
+    if selector is None:
+        raise RuntimeError("NOSA LeanSelect selector was not initialized")
+    lens_c = list(c_lengths) if c_lengths is not None else ops.host_lengths(compressed_cu_seqlens)
+    lens_q = list(q_lengths) if q_lengths is not None else ops.host_lengths(cu_seqlens_q)
+    weights = selector.kernel_weights()
+    ks = ops.project_atom_keys(compressed_k, weights.wk_t)
+    out = ops.atom_scores(query_layer, weights, ks, cu_seqlens_q, compressed_cu_seqlens,
+                          int(max(lens_q, default=0)), int(max(lens_c, default=0)))
+    return out if query_layer.dtype == torch.bfloat16 else out.to(query_layer.dtype)
+
+
 def infllmv2_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
                               dropout_p: float = 0.0, softmax_scale=None, causal: bool = False,
                               window_size=(-1, -1), softcap: float = 0.0, alibi_slopes=None,

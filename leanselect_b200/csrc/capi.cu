@@ -268,6 +268,34 @@ int ls_score_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
   return err == cudaSuccess ? LS_OK : cuda_fail(err, "score_pages launch");
 }
 
+int ls_atom_scores(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                   const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_c, int32_t batch,
+                   int32_t max_seqlen_q, int64_t total_q, int64_t total_c, int32_t num_heads,
+                   int32_t num_kv_heads, int32_t head_dim, int32_t width, int32_t max_atoms,
+                   uint16_t* atom_scores, int32_t* status, void* stream) {
+  int rc = check_score_common(q, wq_t, total_q, num_heads, num_kv_heads, head_dim, width);
+  if (rc != LS_OK) return rc;
+  LS_REQUIRE(cu_seqlens_q && cu_seqlens_c, "null cu_seqlens");
+  LS_REQUIRE(batch >= 1 && max_seqlen_q >= 0 && total_c >= 0 && max_atoms >= 0, "bad sizes");
+  if (total_q == 0 || max_seqlen_q == 0 || max_atoms == 0) return LS_OK;
+  LS_REQUIRE(atom_scores, "null atom_scores");
+  LS_REQUIRE(total_c == 0 || ks, "null ks");
+  if (ks) LS_REQUIRE_ALIGNED(ks);
+  LS_REQUIRE_ALIGNED(atom_scores);
+  ScoreArgs a{};
+  rc = build_score_args(&a, q, wq_t, ks, total_q, total_c, num_heads, num_kv_heads);
+  if (rc != LS_OK) return rc;
+  a.cu_q = cu_seqlens_q;
+  a.cu_c = cu_seqlens_c;
+  a.batch = batch;
+  a.max_seqlen_q = max_seqlen_q;
+  a.max_atoms = max_atoms;
+  a.atom_out = atom_scores;
+  a.status = status;
+  const cudaError_t err = launch_score(kModeAtoms, a, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? LS_OK : cuda_fail(err, "atom_scores launch");
+}
+
 size_t ls_select_pages_workspace_bytes(int64_t total_q, int32_t num_kv_heads,
                                        int32_t max_seqlen_q) {
   if (total_q <= 0 || num_kv_heads <= 0 || max_seqlen_q <= 0) return 0;

@@ -26,7 +26,7 @@ cudaError_t launch_project_atom_keys(const uint16_t* kc, int64_t total_c, int G,
                                      const uint16_t* wk_t, uint16_t* ks, cudaStream_t stream);
 
 // Score/select kernel family (score_select.cu).
-enum ScoreMode { kModeProject = 0, kModeScore = 1, kModeSelect = 2 };
+enum ScoreMode { kModeProject = 0, kModeScore = 1, kModeSelect = 2, kModeAtoms = 3 };
 
 struct ScoreArgs {
   CUtensorMap tm_q;    // Q as [total_q, H*D] bf16, box {64, 128}, 128B swizzle
@@ -48,6 +48,8 @@ struct ScoreArgs {
   int seq_len;         // chunk mode: length of the whole sequence (0 = rows are the sequence)
   int32_t* topk_idx;   // kModeSelect
   float* workspace;    // kModeSelect: pooled page scores [G, total_q, round8(max_pages)]
+  uint16_t* atom_out;  // kModeAtoms: raw atom scores [G, total_q, max_atoms] bf16
+  int max_atoms;       // kModeAtoms: row length of atom_out
   float* page_scores;  // kModeScore
   uint16_t* qs_out;    // kModeProject: [G, total_q, F] bf16
   int32_t* status;

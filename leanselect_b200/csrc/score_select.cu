@@ -16,8 +16,10 @@
 //            into pages (window 5, stride 4, pad 1; a6, pages.py:146-187),
 //            32 pages per atom tile, written as fp32 either to the caller's
 //            page-score output (score mode) or to the selection workspace
-//            (select mode).  In select mode only the atom tiles that can
-//            reach a candidate page of the tile's last row are computed.
+//            (select mode); atom mode instead writes the raw bf16 atom
+//            scores (NOSA's precomputed scores).  In select mode only the atom
+//            tiles that can reach a candidate page of the tile's last row are
+//            computed.
 //
 // topk_kernel (select mode, a7 minicpm.py:3124-3141): one warp per (group,
 // query row) reads the row's candidate pages (visible, not forced) from the
@@ -104,7 +106,7 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
     ti.pos0 = args.pos_offset;
     ti.pages = ((args.seq_len > 0 ? args.seq_len : ti.n) + 63) / 64;
     int needed_atoms = 0;
-    if (MODE == kModeScore) {
+    if (MODE == kModeScore || MODE == kModeAtoms) {
       needed_atoms = ti.atoms;
     } else if (MODE == kModeSelect) {
       // Candidates of the last row are pages p <= qp_max - local - 1, whose
@@ -119,6 +121,14 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
   // (such rows have no candidates, so the top-k kernel reads nothing).
   // Score mode: a sequence without atoms scores -inf everywhere.
   if (!ti.prologue) {
+    if (MODE == kModeAtoms) {
+      const int64_t count = static_cast<int64_t>(ti.rows) * args.max_atoms;
+      for (int64_t i = threadIdx.x; i < count; i += blockDim.x) {
+        const int64_t q_row = ti.q0 + ti.row0 + i / args.max_atoms;
+        args.atom_out[(static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_atoms +
+                      i % args.max_atoms] = 0xFF80u;  // bf16 -inf
+      }
+    }
     if (MODE == kModeScore) {
       const int64_t count = static_cast<int64_t>(ti.rows) * args.max_pages;
       for (int64_t i = threadIdx.x; i < count; i += blockDim.x) {
@@ -299,6 +309,10 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
 
       float* out_row = (MODE == kModeScore ? args.page_scores : args.workspace) +
                        (static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_pages;
+      uint16_t* atom_row = MODE == kModeAtoms
+                               ? args.atom_out +
+                                     (static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_atoms
+                               : nullptr;
       float carry = -INFINITY;  // score of the last atom of the previous tile
       const int last_atom = ti.atoms - 1;
       for (int j = 0; j < ti.atom_tiles && ok; ++j) {
@@ -314,35 +328,61 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             if (a_base + i > last_atom) v[i] = -INFINITY;
-          float pg[8];
+          if constexpr (MODE == kModeAtoms) {
+            // Raw atom scores, rounded to bf16 (the reference's bf16 einsum output).
+            if (valid && a_base < args.max_atoms) {
+              if ((args.max_atoms & 7) == 0) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float m = i == 0 ? carry : v[4 * i - 1];
-            pg[i] = fmaxf(m, fmaxf(fmaxf(v[4 * i], v[4 * i + 1]), fmaxf(v[4 * i + 2], v[4 * i + 3])));
-          }
-          carry = v[31];
-          const int p0 = j * 32 + q * 8;
-          if (valid && p0 < args.max_pages) {
-            if (MODE == kModeScore) {
+                for (int c = 0; c < 4; ++c) {
+                  uint4 u;
+                  u.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
+                  u.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
+                  u.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
+                  u.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
+                  if (a_base + 8 * c < args.max_atoms)
+                    *reinterpret_cast<uint4*>(atom_row + a_base + 8 * c) = u;
+                }
+              } else {
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
-                if (p0 + i >= ti.pages) pg[i] = -INFINITY;
+                for (int i = 0; i < 32; ++i)
+                  if (a_base + i < args.max_atoms)
+                    atom_row[a_base + i] = __bfloat16_as_ushort(__float2bfloat16_rn(v[i]));
+              }
             }
-            if ((args.max_pages & 7) == 0) {
-              // Workspace rows (select mode) are padded to 8 pages: 32-byte stores.
-              *reinterpret_cast<float4*>(out_row + p0) = make_float4(pg[0], pg[1], pg[2], pg[3]);
-              *reinterpret_cast<float4*>(out_row + p0 + 4) = make_float4(pg[4], pg[5], pg[6], pg[7]);
-            } else {
+          } else {
+            float pg[8];
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
-                if (p0 + i < args.max_pages) out_row[p0 + i] = pg[i];
+            for (int i = 0; i < 8; ++i) {
+              const float m = i == 0 ? carry : v[4 * i - 1];
+              pg[i] = fmaxf(m, fmaxf(fmaxf(v[4 * i], v[4 * i + 1]), fmaxf(v[4 * i + 2], v[4 * i + 3])));
+            }
+            carry = v[31];
+            const int p0 = j * 32 + q * 8;
+            if (valid && p0 < args.max_pages) {
+              if (MODE == kModeScore) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  if (p0 + i >= ti.pages) pg[i] = -INFINITY;
+              }
+              if ((args.max_pages & 7) == 0) {
+                // Workspace rows (select mode) are padded to 8 pages: 32-byte stores.
+                *reinterpret_cast<float4*>(out_row + p0) = make_float4(pg[0], pg[1], pg[2], pg[3]);
+                *reinterpret_cast<float4*>(out_row + p0 + 4) = make_float4(pg[4], pg[5], pg[6], pg[7]);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  if (p0 + i < args.max_pages) out_row[p0 + i] = pg[i];
+              }
             }
           }
         }
         tc_fence_before();
         mbar_arrive(&bars->s_empty[buf]);
       }
-      if (valid && ok) {
+      if (MODE == kModeAtoms && valid && ok) {
+        for (int a = ti.atom_tiles * 128; a < args.max_atoms; ++a) atom_row[a] = 0xFF80u;
+      }
+      if (MODE != kModeAtoms && valid && ok) {
         // Pages past the last computed tile: only page 32*tiles can still see
         // an atom (the last one, carried).  Score mode fills the whole row;
         // select mode fills up to the row's last candidate page.
@@ -537,6 +577,12 @@ cudaError_t launch_score(int mode, const ScoreArgs& args_in, cudaStream_t stream
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
       if (err != cudaSuccess) return err;
       score_kernel<kModeScore><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
+      break;
+    case kModeAtoms:
+      err = cudaFuncSetAttribute(score_kernel<kModeAtoms>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (err != cudaSuccess) return err;
+      score_kernel<kModeAtoms><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
       break;
     case kModeSelect: {
       // Workspace rows are padded to a multiple of 8 pages (32-byte aligned stores).

@@ -28,7 +28,8 @@ import functools
 import types
 
 from .attention import (CompressK, infllmv2_attn_stage1, infllmv2_attn_varlen_func,
-                        lightweight_compressed_attention, max_pooling_1d_varlen)
+                        lightweight_compressed_attention, max_pooling_1d_varlen,
+                        nosa_atom_scores)
 from .selector import LeanSelectSelector
 
 ATTENTION_CLASS_NAMES = ("MiniCPMInfLLMv2Attention",)
@@ -72,10 +73,13 @@ def patch_attention(attn) -> None:
 
 
 def patch_selector_owner(owner) -> None:
-    """Swap ``owner.leanselect`` for the B200 selector (shared parameters)."""
+    """Swap ``owner.leanselect`` for the B200 selector (shared parameters); on
+    NOSA layers also route ``_leanselect_atom_scores`` to the atom-score kernel."""
     sel = getattr(owner, "leanselect", None)
     if sel is not None and not isinstance(sel, LeanSelectSelector):
         owner.leanselect = LeanSelectSelector.from_reference(sel)
+    if hasattr(owner, "_leanselect_atom_scores"):
+        owner._leanselect_atom_scores = functools.partial(nosa_atom_scores, owner)
 
 
 def install(model) -> int:

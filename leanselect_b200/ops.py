@@ -253,6 +253,27 @@ def score_pages(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
     return out
 
 
+def atom_scores(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
+                cu_seqlens_q: torch.Tensor, cu_seqlens_c: torch.Tensor, max_seqlen_q: int,
+                max_atoms: int) -> torch.Tensor:
+    """Raw atom scores ``[G, total_q, max_atoms]`` bf16 (-inf past each sequence's atoms)."""
+    dev = _require_cuda(q, ks, cu_seqlens_q, cu_seqlens_c)
+    qb = _bf16(q)
+    total_q = qb.shape[0]
+    G = weights.num_kv_heads
+    total_c = ks.shape[1]
+    out = torch.empty(G, total_q, int(max_atoms), dtype=torch.bfloat16, device=dev)
+    if total_q == 0 or max_atoms == 0:
+        return out
+    cu_q, cu_c = _i32(cu_seqlens_q), _i32(cu_seqlens_c)
+    _native.call("ls_atom_scores", qb.data_ptr(), weights.wq_t.data_ptr(),
+                 _ptr(ks) if total_c else None, cu_q.data_ptr(), cu_c.data_ptr(),
+                 cu_q.numel() - 1, int(max_seqlen_q), total_q, total_c, weights.num_heads, G,
+                 weights.head_dim, weights.width, int(max_atoms), out.data_ptr(),
+                 status_word(dev).data_ptr(), _stream(dev))
+    return out
+
+
 def select_pages(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
                  cu_seqlens_q: torch.Tensor, cu_seqlens_c: torch.Tensor, max_seqlen_q: int, *,
                  take: int, init_blocks: int = 1, local_blocks: int = 2, block_size: int = 64,

@@ -397,3 +397,26 @@ def test_per_sequence_budgets_match_oracle():
         assert not bad, bad[:3]
     ref, _ = ora.sparse_attention(inp.q, inp.k, inp.v, inp.cu_seqlens, inp.cu_seqlens, idx)
     _attn_check(out, None, ref, None)
+
+
+def test_nosa_atom_scores_match_oracle():
+    """Raw atom scores for NOSA's precomputed-score path (nosa.py:1822-1853)."""
+    lens = [900, 20, 1333]
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=3, seed=97, bf16=True)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    sel = selector_for(inp.params)
+    module = type("NosaLayer", (), {"leanselect": sel})()
+    got = lsb.nosa_atom_scores(module, to_dev(inp.q), to_dev(kc), cu_dev(inp.cu_seqlens),
+                               cu_dev(cu_c)).float().cpu().numpy()
+    max_atoms = int(np.diff(cu_c).max())
+    assert got.shape == (2, sum(lens), max_atoms)
+    qf, kf = ora.fold_weights(inp.params, "bf16")
+    for b, n in enumerate(lens):
+        q0, c0, c1 = inp.cu_seqlens[b], cu_c[b], cu_c[b + 1]
+        rows = got[:, q0:q0 + n]
+        if c1 > c0:
+            want = ora.atom_scores(ora.project_queries(inp.q[q0:q0 + n], qf, 2, "bf16"),
+                                   ora.project_atom_keys(kc[c0:c1], kf, "bf16"))
+            np.testing.assert_allclose(rows[..., :c1 - c0], want, rtol=2 ** -7, atol=2e-3)
+        assert np.all(np.isneginf(rows[..., c1 - c0:]))

@@ -40,6 +40,9 @@ class NosaAttention(nn.Module):
         super().__init__()
         self.leanselect = RefSelector()
 
+    def _leanselect_atom_scores(self, *args):  # replaced by install()
+        raise AssertionError("reference path should have been patched")
+
 
 def test_install_patches_every_attention_module():
     model = nn.ModuleList([MiniCPMInfLLMv2Attention(), MiniCPMInfLLMv2Attention(), NosaAttention()])
@@ -52,6 +55,7 @@ def test_install_patches_every_attention_module():
         assert attn._lightweight_compressed_attention.func is lsb.lightweight_compressed_attention
         assert isinstance(attn.sparse_forward, types.MethodType)
     assert isinstance(model[2].leanselect, lsb.LeanSelectSelector)
+    assert model[2]._leanselect_atom_scores.func is lsb.nosa_atom_scores
     # The selectors share the reference parameter tensors (checkpoints keep working).
     for m, p in zip(model, ref_params):
         assert m.leanselect.head_mix is p
