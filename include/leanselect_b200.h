@@ -212,6 +212,33 @@ int ls_select_pages_noalloc(const uint16_t* q, const uint16_t* wq_t, const uint1
                             int32_t* topk_idx, int32_t* status, void* stream);
 
 /*
+ * ls_uniform_select_pages -- replaces uniform_prefill_topk_idx
+ * (leanselect/ops/uniform.py:185-320), the uniform-method selection that
+ * MiniCPMInfLLMv2Attention._lightweight_compressed_attention dispatches to
+ * when selection_method == "uniform" (minicpm.py:3073-3087).  Scores are
+ * mean(group query heads) . Kc * softmax_scale (0 = head_dim^-0.5), kept
+ * in bf16 like the reference's bf16 matmul (head_mix.py:21-77); atoms after
+ * the query are hidden, pages max-pooled, sink + local pages forced, and
+ * the top `take` = min(topk, max pages) taken over all pages, a pick of
+ * page q_page+1 leaving its slot -1 (uniform.py:68-112).  kc is the
+ * compressed-key tensor [total_c, G, D] bf16 itself.  Rows are written sink
+ * pages, selected pages, local pages -- ascending -- then -1 (the
+ * reference orders by score; the sets are the same).  `workspace` holds
+ * ls_uniform_select_workspace_bytes(...) bytes.  The reference rejects query
+ * lengths <= 1 on the host; this entry point does not look at them.
+ */
+size_t ls_uniform_select_workspace_bytes(int64_t total_q, int64_t total_c, int32_t num_heads,
+                                         int32_t num_kv_heads, int32_t max_seqlen_q);
+int ls_uniform_select_pages(const uint16_t* q, const uint16_t* kc, const int32_t* cu_seqlens_q,
+                            const int32_t* cu_seqlens_c, int32_t batch, int32_t max_seqlen_q,
+                            int64_t total_q, int64_t total_c, int32_t num_heads,
+                            int32_t num_kv_heads, int32_t head_dim, int32_t take,
+                            int32_t init_blocks, int32_t local_blocks, int32_t block_size,
+                            int32_t kernel_stride, float softmax_scale, int32_t* topk_idx,
+                            void* workspace, size_t workspace_bytes, int32_t* status,
+                            void* stream);
+
+/*
  * ls_select_pages_chunk -- ls_select_pages for a slice of ONE sequence, used
  * by the sequence-parallel prefill (no reference counterpart: the reference
  * prefill runs on one GPU).  q holds chunk_q query rows at positions

@@ -11,10 +11,11 @@ from .attention import (CompressK, LayerConfig, infllmv2_attn_varlen_func,
                         lightweight_compressed_attention, nosa_atom_scores,
                         prefill_layer_attention)
 from .selector import LeanSelectSelector
+from .uniform import uniform_prefill_topk_idx
 
 __all__ = [
     "ops", "LeanSelectError", "LS_MAX_TOPK", "version", "CompressK", "LayerConfig",
     "infllmv2_attn_varlen_func", "lightweight_compressed_attention", "nosa_atom_scores",
     "prefill_layer_attention",
-    "LeanSelectSelector",
+    "LeanSelectSelector", "uniform_prefill_topk_idx",
 ]

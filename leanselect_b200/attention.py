@@ -68,11 +68,19 @@ def lightweight_compressed_attention(module, q_unpad: torch.Tensor, k_compressed
     if cache_lens is not None:
         raise ValueError("Lightweight selection is prefill only")
     method = getattr(module, "selection_method", "leanselect")
+    lengths = list(q_lengths) if q_lengths is not None else ops.host_lengths(cu_seqlens_q)
+    if method == "uniform":
+        # minicpm.py:3073-3087
+        from .uniform import uniform_prefill_topk_idx
+        return uniform_prefill_topk_idx(
+            q_unpad, k_compressed, cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
+            max_seqlen_q=max_seqlen_q, topk=int(module.topk), block_size=int(module.block_size),
+            kernel_stride=int(module.kernel_stride), init_blocks=int(module.init_blocks),
+            local_blocks=int(module.local_blocks), q_lengths=lengths)[0]
     if method != "leanselect":
         raise NotImplementedError(f"selection_method={method!r} is not served by leanselect_b200")
     selector = _as_selector(module)
     block = int(module.block_size)
-    lengths = list(q_lengths) if q_lengths is not None else ops.host_lengths(cu_seqlens_q)
     max_pages = max(((n + block - 1) // block for n in lengths), default=0)
     take = min(int(module.topk), max_pages)
     weights = selector.kernel_weights()

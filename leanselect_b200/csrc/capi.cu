@@ -345,6 +345,83 @@ int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
   return err == cudaSuccess ? LS_OK : cuda_fail(err, "select_pages launch");
 }
 
+namespace {
+size_t align256(size_t n) { return (n + 255) & ~size_t{255}; }
+}  // namespace
+
+size_t ls_uniform_select_workspace_bytes(int64_t total_q, int64_t total_c, int32_t num_heads,
+                                         int32_t num_kv_heads, int32_t max_seqlen_q) {
+  if (total_q <= 0 || total_c < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_seqlen_q <= 0)
+    return 0;
+  const size_t weights = sizeof(uint16_t) * static_cast<size_t>(num_heads) * 128 * 128;
+  const size_t keys = sizeof(uint16_t) * static_cast<size_t>(num_kv_heads) *
+                      static_cast<size_t>(std::max<int64_t>(total_c, 1)) * 128;
+  return align256(weights) + align256(keys) +
+         ls_select_pages_workspace_bytes(total_q, num_kv_heads, max_seqlen_q);
+}
+
+int ls_uniform_select_pages(const uint16_t* q, const uint16_t* kc, const int32_t* cu_seqlens_q,
+                            const int32_t* cu_seqlens_c, int32_t batch, int32_t max_seqlen_q,
+                            int64_t total_q, int64_t total_c, int32_t num_heads,
+                            int32_t num_kv_heads, int32_t head_dim, int32_t take,
+                            int32_t init_blocks, int32_t local_blocks, int32_t block_size,
+                            int32_t kernel_stride, float softmax_scale, int32_t* topk_idx,
+                            void* workspace, size_t workspace_bytes, int32_t* status,
+                            void* stream) {
+  LS_REQUIRE(q && cu_seqlens_q && cu_seqlens_c, "null argument");
+  LS_REQUIRE(total_q >= 0 && total_q < (int64_t{1} << 31), "total_q out of range");
+  LS_REQUIRE(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
+             "num_heads must be a positive multiple of num_kv_heads");
+  if (head_dim != 128) return fail(LS_ERR_UNSUPPORTED, "head_dim must be 128");
+  const int hg = num_heads / num_kv_heads;
+  if (hg != 8 && hg != 16) return fail(LS_ERR_UNSUPPORTED, "heads per group must be 8 or 16");
+  LS_REQUIRE(batch >= 1 && max_seqlen_q >= 0 && total_c >= 0, "bad sizes");
+  LS_REQUIRE(take >= 0 && init_blocks >= 0 && local_blocks >= 0, "negative budget");
+  LS_REQUIRE(softmax_scale >= 0.f, "negative softmax_scale");
+  if (block_size != 64 || kernel_stride != 16)
+    return fail(LS_ERR_UNSUPPORTED, "block_size must be 64 and kernel_stride 16");
+  if (take > LS_MAX_TOPK) return fail(LS_ERR_UNSUPPORTED, "take exceeds LS_MAX_TOPK");
+  if (max_seqlen_q > 65536 * 64)
+    return fail(LS_ERR_UNSUPPORTED, "sequences longer than 4M tokens are not supported");
+  LS_REQUIRE_ALIGNED(q);
+  if (total_q == 0 || take == 0) return LS_OK;
+  LS_REQUIRE(topk_idx, "null topk_idx");
+  LS_REQUIRE(total_c == 0 || kc, "null kc");
+  if (kc) LS_REQUIRE_ALIGNED(kc);
+  const size_t need = ls_uniform_select_workspace_bytes(total_q, total_c, num_heads,
+                                                        num_kv_heads, max_seqlen_q);
+  LS_REQUIRE(workspace && workspace_bytes >= need, "workspace too small: %zu < %zu bytes",
+             workspace_bytes, need);
+  LS_REQUIRE_ALIGNED(workspace);
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  uint16_t* wq_t = reinterpret_cast<uint16_t*>(base);
+  base += align256(sizeof(uint16_t) * static_cast<size_t>(num_heads) * 128 * 128);
+  uint16_t* ks = reinterpret_cast<uint16_t*>(base);
+  base += align256(sizeof(uint16_t) * static_cast<size_t>(num_kv_heads) *
+                   static_cast<size_t>(std::max<int64_t>(total_c, 1)) * 128);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t err = launch_uniform_prep(kc, total_c, num_kv_heads, hg, wq_t, ks, st);
+  if (err != cudaSuccess) return cuda_fail(err, "uniform prep launch");
+  ScoreArgs a{};
+  int rc = build_score_args(&a, q, wq_t, ks, total_q, total_c, num_heads, num_kv_heads);
+  if (rc != LS_OK) return rc;
+  a.workspace = reinterpret_cast<float*>(base);
+  a.cu_q = cu_seqlens_q;
+  a.cu_c = cu_seqlens_c;
+  a.batch = batch;
+  a.max_seqlen_q = max_seqlen_q;
+  a.take = take;
+  a.init_blocks = init_blocks;
+  a.local_blocks = local_blocks;
+  a.max_pages = (max_seqlen_q + 63) / 64;
+  a.topk_idx = topk_idx;
+  a.status = status;
+  a.uniform = 1;
+  a.score_scale = softmax_scale > 0.f ? softmax_scale : 0.08838834764831845f;  // 128^-0.5
+  err = launch_score(kModeSelect, a, st);
+  return err == cudaSuccess ? LS_OK : cuda_fail(err, "uniform select launch");
+}
+
 int ls_select_pages_chunk(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
                           int64_t chunk_q, int32_t q_position, int32_t seq_len, int64_t total_c,
                           int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t width,

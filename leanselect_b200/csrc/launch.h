@@ -53,9 +53,21 @@ struct ScoreArgs {
   float* page_scores;  // kModeScore
   uint16_t* qs_out;    // kModeProject: [G, total_q, F] bf16
   int32_t* status;
+  // kModeSelect, uniform method (ops/uniform.py): atoms after the query are
+  // hidden, pooled scores are rounded as bf16(bf16(s) * score_scale), rows
+  // of sequences without atoms keep their forced pages, and page q_page+1
+  // competes for a slot that it then leaves empty.
+  int uniform;
+  float score_scale;
 };
 
 cudaError_t launch_score(int mode, const ScoreArgs& args, cudaStream_t stream);
+
+// Uniform method inputs (prep.cu): the mean-of-group-heads projection as a
+// folded weight wq_t [G, D, Hg*D] (1/Hg on the diagonal of each head block)
+// and Kc [total_c, G, D] re-laid out as Ks [G, total_c, D].
+cudaError_t launch_uniform_prep(const uint16_t* kc, int64_t total_c, int num_kv_heads, int hg,
+                                uint16_t* wq_t, uint16_t* ks, cudaStream_t stream);
 
 // Floats of selection workspace for `rows` = G * query rows and `max_pages`.
 size_t select_workspace_floats(int64_t rows, int max_pages);

@@ -227,8 +227,56 @@ __global__ void __launch_bounds__(256) project_atom_keys_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Uniform method inputs (ops/uniform.py, pages.py:62-71)
+// ---------------------------------------------------------------------------
+
+// One pass of 16-byte vectors: the first `w_vecs` write the mean-query
+// weight wq_t[g, f, s*D + d] = (d == f) / Hg, the rest copy Kc[a, g, :] to
+// Ks[g, a, :].  With Hg a power of two, Q x wq_t is the exact group mean
+// before its bf16 rounding, which is how the reference's bf16 mean rounds.
+__global__ void __launch_bounds__(256) uniform_prep_kernel(const uint4* __restrict__ kc,
+                                                           int64_t total_c, int G, int hg,
+                                                           uint4* __restrict__ wq_t,
+                                                           uint4* __restrict__ ks) {
+  constexpr int D = 128, V = D / 8;
+  const int64_t w_vecs = static_cast<int64_t>(G) * D * hg * V;
+  const int64_t k_vecs = total_c * G * V;
+  const uint16_t inv = __bfloat16_as_ushort(__float2bfloat16_rn(1.0f / static_cast<float>(hg)));
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < w_vecs + k_vecs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (i < w_vecs) {
+      const int f = static_cast<int>((i / (static_cast<int64_t>(hg) * V)) % D);
+      const int d0 = static_cast<int>(i % V) * 8;  // d of the vector's first element
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+      if (f >= d0 && f < d0 + 8) {
+        const int e = f - d0;
+        w[e >> 1] = static_cast<uint32_t>(inv) << (16 * (e & 1));
+      }
+      wq_t[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      const int64_t j = i - w_vecs;
+      const int c = static_cast<int>(j % V);
+      const int64_t ag = j / V;  // a * G + g
+      const int64_t a = ag / G;
+      const int g = static_cast<int>(ag % G);
+      ks[(static_cast<int64_t>(g) * total_c + a) * V + c] = kc[j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
+
+cudaError_t launch_uniform_prep(const uint16_t* kc, int64_t total_c, int num_kv_heads, int hg,
+                                uint16_t* wq_t, uint16_t* ks, cudaStream_t stream) {
+  const int64_t vecs = (static_cast<int64_t>(num_kv_heads) * 128 * hg + total_c * num_kv_heads) * 16;
+  const int blocks = static_cast<int>(std::min<int64_t>((vecs + 255) / 256, 148 * 8));
+  uniform_prep_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const uint4*>(kc), total_c,
+                                                  num_kv_heads, hg, reinterpret_cast<uint4*>(wq_t),
+                                                  reinterpret_cast<uint4*>(ks));
+  return cudaGetLastError();
+}
 
 cudaError_t launch_fold_weights(const float* head_mix, const float* kv_head_mix,
                                 const float* q_proj, const float* k_proj, int H, int G, int D,

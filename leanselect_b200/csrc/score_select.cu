@@ -82,6 +82,14 @@ struct TileInfo {
   bool prologue;    // whether Qs is computed at all
 };
 
+// Uniform method page score: the reference's bf16 matmul output times the
+// softmax scale, rounded to bf16 again (head_mix.py:47-53, bf16 inputs).
+// Pooling commutes with this monotone map, so it is applied per page.
+__device__ __forceinline__ float uniform_score(float s, float scale) {
+  const float r = __bfloat162float(__float2bfloat16_rn(s));
+  return __bfloat162float(__float2bfloat16_rn(r * scale));
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constant__ ScoreArgs args) {
   const int tiles_max = (args.max_seqlen_q + kRows - 1) / kRows;
@@ -95,6 +103,11 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
     ti.q0 = args.cu_q ? __ldg(args.cu_q + ti.b) : 0;
     ti.n = args.cu_q ? static_cast<int>(__ldg(args.cu_q + ti.b + 1) - ti.q0) : args.max_seqlen_q;
     ti.row0 = ti.tile * kRows;
+    if (ti.n > args.max_seqlen_q) {
+      // max_seqlen_q sizes the workspace rows: a longer sequence is a caller error.
+      if (ti.tile == 0 && threadIdx.x == 0) report(args.status, LS_DEVERR_SEQLENS);
+      return;
+    }
     if (ti.row0 >= ti.n) return;  // whole CTA exits before touching barriers or TMEM
     ti.rows = min(kRows, ti.n - ti.row0);
     // Null cu_seqlens_c: one sequence whose atoms are all total_c rows of Ks.
@@ -110,9 +123,11 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
       needed_atoms = ti.atoms;
     } else if (MODE == kModeSelect) {
       // Candidates of the last row are pages p <= qp_max - local - 1, whose
-      // windows end at atom 4p + 3 < 4 (qp_max - local).
+      // windows end at atom 4p + 3 < 4 (qp_max - local).  Uniform method:
+      // also page qp_max + 1, whose only visible atom is 4 qp_max + 3.
       const int qp_max = (ti.pos0 + ti.row0 + ti.rows - 1) / 64;
-      needed_atoms = max(0, min(ti.atoms, 4 * (qp_max - args.local_blocks)));
+      needed_atoms = args.uniform ? min(ti.atoms, 4 * qp_max + 4)
+                                  : max(0, min(ti.atoms, 4 * (qp_max - args.local_blocks)));
     }
     ti.atom_tiles = (needed_atoms + kRows - 1) / kRows;
     ti.prologue = (MODE == kModeProject) || ti.atom_tiles > 0;
@@ -269,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
     const int row = quad * 32 + lane;
     const bool valid = row < ti.rows;
     const int64_t q_row = ti.q0 + ti.row0 + row;     // packed row
+    const int pos = ti.pos0 + ti.row0 + row;          // position inside the sequence
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     bool ok = mbar_wait(&bars->qs_full, 0, status, abort_flag);
     tc_fence_after();
@@ -328,6 +344,12 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             if (a_base + i > last_atom) v[i] = -INFINITY;
+          if (MODE == kModeSelect && args.uniform) {
+            // Atom a starts at token 16 a and is visible iff 16 a <= pos (pages.py:199-219).
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (16 * (a_base + i) > pos) v[i] = -INFINITY;
+          }
           if constexpr (MODE == kModeAtoms) {
             // Raw atom scores, rounded to bf16 (the reference's bf16 einsum output).
             if (valid && a_base < args.max_atoms) {
@@ -357,6 +379,10 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
               pg[i] = fmaxf(m, fmaxf(fmaxf(v[4 * i], v[4 * i + 1]), fmaxf(v[4 * i + 2], v[4 * i + 3])));
             }
             carry = v[31];
+            if (MODE == kModeSelect && args.uniform) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) pg[i] = uniform_score(pg[i], args.score_scale);
+            }
             const int p0 = j * 32 + q * 8;
             if (valid && p0 < args.max_pages) {
               if (MODE == kModeScore) {
@@ -386,11 +412,21 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
         // Pages past the last computed tile: only page 32*tiles can still see
         // an atom (the last one, carried).  Score mode fills the whole row;
         // select mode fills up to the row's last candidate page.
-        const int qp = (ti.pos0 + ti.row0 + row) / 64;
+        const int qp = pos / 64;
         const int end = MODE == kModeScore ? args.max_pages
+                        : args.uniform     ? min(args.max_pages, qp + 2)
                                            : min(args.max_pages, qp - args.local_blocks);
+        const float tail = (MODE == kModeSelect && args.uniform)
+                               ? uniform_score(carry, args.score_scale) : carry;
         for (int p = ti.atom_tiles * 32; p < end; ++p)
-          out_row[p] = (p == ti.atom_tiles * 32 && p < ti.pages) ? carry : -INFINITY;
+          out_row[p] = (p == ti.atom_tiles * 32 && p < ti.pages) ? tail : -INFINITY;
+        if (MODE == kModeSelect && args.uniform && qp + 1 < ti.pages && qp + 1 < args.max_pages) {
+          // Page qp+1 competes as the candidate after the last regular one:
+          // move its score into that slot (the first non-sink local page,
+          // whose own score is never read; the same thread wrote both).
+          const int slot = max(max(0, qp - args.local_blocks), min(args.init_blocks, qp + 1));
+          out_row[slot] = out_row[qp + 1];
+        }
       }
     }
   }
@@ -431,6 +467,10 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
       b = find_sequence(args.cu_q, args.batch, q_row);
       q0 = __ldg(args.cu_q + b);
       n = static_cast<int>(__ldg(args.cu_q + b + 1) - q0);
+      if (n > args.max_seqlen_q) {  // reported by score_kernel; the row stays empty
+        for (int k = lane; k < args.take; k += 32) args.topk_idx[r * args.take + k] = -1;
+        continue;
+      }
     } else {
       n = args.max_seqlen_q;
     }
@@ -449,13 +489,26 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
     const int local0 = max(lo, n_init);
     const int n_local = qp - local0 + 1;                 // local pages that are not sinks
     const int n_forced = n_init + n_local;
-    const int m = max(0, lo - n_init);                   // candidates n_init .. lo-1
-    const int cap = max(0, min(take_b - n_forced, m));
-    if (atoms <= 0) {
+    int m = max(0, lo - n_init);                         // candidates n_init .. lo-1
+    int slots = take_b - n_forced;
+    // Uniform method: page qp+1 is scored too (its first window atom may be
+    // visible) and competes as candidate m, or as a forced sink; either way
+    // a slot it wins stays -1 (uniform.py:100-106).  Rows of sequences
+    // without atoms keep their forced pages (head_mix.py:150-170).
+    int future = -1;
+    if (args.uniform) {
+      if (atoms <= 0) m = 0;
+      slots -= max(0, min(args.init_blocks, pages) - (qp + 1));  // future sinks
+      if (atoms > 0 && qp + 1 < pages && qp + 1 >= args.init_blocks) future = m;
+    } else if (atoms <= 0) {
       // The reference leaves rows of sequences without atoms at -1 (minicpm.py:3115-3116).
       for (int k = lane; k < args.take; k += 32) out[k] = -1;
       continue;
     }
+    const int m_all = m + (future >= 0 ? 1 : 0);
+    const int cap = max(0, min(slots, m_all));
+    // Candidate i is page n_init + i; candidate m (page qp+1) was stored by
+    // the score kernel in slot n_init + m, the first non-sink local page.
     const int sinks_out = min(n_init, take_b);
     for (int k = lane; k < sinks_out; k += 32) out[k] = k;
 
@@ -465,7 +518,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
     int valid_total = 0;
     if (cap > 0) {
       // Count finite candidates first: if all fit, no selection is needed.
-      for (int i = lane; i < m; i += 32) valid_total += score_key(scores[n_init + i]) != 0u;
+      for (int i = lane; i < m_all; i += 32) valid_total += score_key(scores[n_init + i]) != 0u;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) valid_total += __shfl_xor_sync(0xffffffffu, valid_total, o);
     }
@@ -476,7 +529,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
         const int shift = 24 - 8 * pass;
         for (int k = lane; k < 256; k += 32) hist[k] = 0;
         __syncwarp();
-        for (int i = lane; i < m; i += 32) {
+        for (int i = lane; i < m_all; i += 32) {
           const uint32_t key = score_key(scores[n_init + i]);
           if (key != 0u && ((key ^ prefix) & mask) == 0) atomicAdd(&hist[(key >> shift) & 255u], 1u);
         }
@@ -526,9 +579,9 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
     int k_out = sinks_out;
     if (cap > 0) {
       int ties_seen = 0;
-      for (int base = 0; base < m; base += 32) {
+      for (int base = 0; base < m_all; base += 32) {
         const int i = base + lane;
-        const uint32_t key = i < m ? score_key(scores[n_init + i]) : 0u;
+        const uint32_t key = i < m_all ? score_key(scores[n_init + i]) : 0u;
         bool take;
         if (select_all) {
           take = key != 0u;
@@ -539,6 +592,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
           take = key > prefix || (tie && tie_rank < need);
           ties_seen += __popc(tie_mask);
         }
+        if (i == future) take = false;  // the slot page qp+1 won stays empty
         const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
         if (take) out[k_out + __popc(take_mask & ((1u << lane) - 1))] = n_init + i;
         k_out += __popc(take_mask);

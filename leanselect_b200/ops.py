@@ -300,6 +300,36 @@ def select_pages(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
     return idx
 
 
+def uniform_select_pages(q: torch.Tensor, kc: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                         cu_seqlens_c: torch.Tensor, max_seqlen_q: int, *, take: int,
+                         init_blocks: int = 1, local_blocks: int = 2, block_size: int = 64,
+                         kernel_stride: int = 16,
+                         softmax_scale: float | None = None) -> torch.Tensor:
+    """Uniform-method selection (ops/uniform.py:185-320): ``[G, total_q, take]`` int32.
+
+    ``kc [total_c, G, D]`` are the compressed keys themselves.
+    """
+    dev = _require_cuda(q, kc, cu_seqlens_q, cu_seqlens_c)
+    qb, kcb = _bf16(q), _bf16(kc)
+    total_q, H, D = qb.shape
+    total_c, G = kcb.shape[0], kcb.shape[1]
+    if take > LS_MAX_TOPK:
+        raise ValueError(f"take={take} exceeds LS_MAX_TOPK={LS_MAX_TOPK}")
+    idx = torch.empty(G, total_q, take, dtype=torch.int32, device=dev)
+    if take == 0 or total_q == 0:
+        return idx
+    cu_q, cu_c = _i32(cu_seqlens_q), _i32(cu_seqlens_c)
+    nbytes = _native.load().ls_uniform_select_workspace_bytes(total_q, total_c, H, G,
+                                                              int(max_seqlen_q))
+    ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=dev)
+    _native.call("ls_uniform_select_pages", qb.data_ptr(), kcb.data_ptr() if total_c else None,
+                 cu_q.data_ptr(), cu_c.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q), total_q,
+                 total_c, H, G, D, int(take), int(init_blocks), int(local_blocks), block_size,
+                 kernel_stride, float(softmax_scale or 0.0), idx.data_ptr(), ws.data_ptr(),
+                 ws.numel(), status_word(dev).data_ptr(), _stream(dev))
+    return idx
+
+
 def _workspace(dev: torch.device, rows: int, groups: int, seq_len: int) -> torch.Tensor:
     """Scratch for the selection kernels, from PyTorch's caching allocator."""
     nbytes = _native.load().ls_select_pages_workspace_bytes(rows, groups, seq_len)

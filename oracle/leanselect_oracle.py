@@ -690,3 +690,172 @@ def synthetic_keys_and_sample(seq_len: int, rows, *, num_heads: int = 32, num_kv
     q += hot_shift * u
     params = selector_params(num_heads, num_kv_heads, head_dim, router_heads, router_dim, rng)
     return bf16_round(q), bf16_round(k), bf16_round(v), params
+
+
+# ----------------------------------------------------------------------------
+# Uniform method: the mean-query head mix (ops/uniform.py, ops/head_mix.py)
+# ----------------------------------------------------------------------------
+
+def uniform_group_queries(q: np.ndarray, num_kv_heads: int, policy: str = "fp32") -> np.ndarray:
+    """``uniform_group_queries`` (pages.py:62-71): mean of each group's heads, ``[N, G, D]``."""
+    q = np.asarray(q, dtype=np.float32)
+    n, h, d = q.shape
+    hg = h // num_kv_heads
+    out = q.reshape(n, num_kv_heads, hg, d).astype(np.float64).mean(axis=2).astype(np.float32)
+    return _maybe_round(out, policy)
+
+
+def uniform_atom_scores(q: np.ndarray, kc: np.ndarray, num_kv_heads: int, *,
+                        softmax_scale: float | None = None, policy: str = "fp32") -> np.ndarray:
+    """Stage-1 scores of the uniform method, ``[G, N, A]`` (head_mix.py:21-77, 80-170).
+
+    ``dots = mean_query . kc`` in the input dtype, then ``* scale`` (default
+    ``D**-0.5``) in the input dtype: under the bf16 policy both the matmul
+    output and the scaled value are rounded to bf16 (torch computes the
+    bf16-tensor-times-scalar product in fp32 and rounds once).
+    """
+    qg = uniform_group_queries(q, num_kv_heads, policy)
+    kc = _maybe_round(np.asarray(kc, dtype=np.float32), policy)
+    d = q.shape[-1]
+    scale = np.float32(float(d) ** -0.5 if softmax_scale is None else float(softmax_scale))
+    dots = np.einsum("ngd,agd->gna", qg.astype(np.float64), kc.astype(np.float64),
+                     optimize=True).astype(np.float32)
+    dots = _maybe_round(dots, policy)
+    return _maybe_round((dots * scale).astype(np.float32), policy)
+
+
+def uniform_select_rows(atoms: np.ndarray, positions, *, seq_len: int, take: int, topk: int,
+                        init_blocks: int, local_blocks: int, block_size: int = 64,
+                        kernel_stride: int = 16):
+    """Masking, pooling and top-k of the uniform method for rows of ONE sequence.
+
+    Restates ``_uniform_prefill_vectorized_topk`` (uniform.py:68-112) and the
+    ragged branch of ``uniform_prefill_topk_idx`` (uniform.py:269-308):
+    atoms whose window starts after the query are ``-inf``
+    (``apply_atom_causal_mask``, pages.py:199-219); pages are max-pooled
+    over ``seq_len``; forced pages (``p < init_blocks`` or
+    ``q_page - local_blocks <= p <= q_page``, pages.py:222-240) are ``+inf``;
+    ``topk(min(topk, P))`` runs over ALL pages and picks beyond the query's
+    page become ``-1`` afterwards.  Such a pick is possible: page
+    ``q_page + 1`` sees its first window atom once the query is within one
+    stride of the page end, and when it makes the cut it takes a slot that
+    no other page gets.  Ties go to the lower page here (the reference's
+    order among equal scores is unspecified).
+
+    ``atoms [G, R, A]`` are the rows' uniform atom scores.  Returns
+    ``(idx [G, R, take] ascending with -1 padding, boundary [G, R],
+    masked page scores [G, R, P])``.
+    """
+    positions = np.asarray(positions, dtype=np.int64)
+    g, r, a = atoms.shape
+    atom_start = np.arange(a) * kernel_stride
+    vis_atoms = atom_start[None, :] <= positions[:, None]
+    masked_atoms = np.where(vis_atoms[None], atoms, NEG_INF).astype(np.float32)
+    pages = pool_atoms_to_pages(masked_atoms, max(seq_len, 1), block_size, kernel_stride)
+    p = pages.shape[-1]
+    qpage = positions // block_size
+    page_ids = np.arange(p)
+    local = (qpage[:, None] >= page_ids[None, :]) & (qpage[:, None] <= page_ids[None, :] + local_blocks)
+    forced = (page_ids < init_blocks)[None, :] | local
+    masked = np.where(forced[None], POS_INF, pages).astype(np.float32)
+    k = min(topk, p)
+    order = np.argsort(-masked, axis=-1, kind="stable")[..., :k]
+    vals = np.take_along_axis(masked, order, axis=-1)
+    finite_vals = np.where(np.isfinite(vals), vals, POS_INF)
+    picked_any = ~np.isneginf(vals)
+    boundary = np.where(picked_any.any(-1), finite_vals.min(-1), np.nan).astype(np.float32)
+    chosen = np.where(order > qpage[None, :, None], -1, order)
+    idx = np.full((g, r, take), -1, dtype=np.int32)
+    big = np.iinfo(np.int32).max
+    srt = np.sort(np.where(chosen < 0, big, chosen), axis=-1)
+    idx[..., :k] = np.where(srt == big, -1, srt).astype(np.int32)
+    return idx, boundary, masked
+
+
+def uniform_prefill_topk_idx(q: np.ndarray, kc: np.ndarray, cu_seqlens_q: np.ndarray,
+                             cu_seqlens_c: np.ndarray, *, topk: int, init_blocks: int = 1,
+                             local_blocks: int = 2, block_size: int = 64, kernel_stride: int = 16,
+                             policy: str = "fp32") -> Selection:
+    """``uniform_prefill_topk_idx`` (uniform.py:185-320) on a packed batch.
+
+    Output width ``min(topk, max_pages)``; each sequence fills
+    ``min(topk, P_b)`` columns.  A sequence without atoms still selects its
+    forced pages (its scores are all ``-inf``, head_mix.py:150-170).  The
+    equal-packed, streaming and ragged branches of the reference compute the
+    same selection; this follows the ragged one.  The reference rejects
+    query lengths <= 1 (uniform.py:203-204).
+    """
+    cu_q = np.asarray(cu_seqlens_q, dtype=np.int64)
+    cu_c = np.asarray(cu_seqlens_c, dtype=np.int64)
+    lens = np.diff(cu_q)
+    if lens.size == 0 or (lens <= 1).any():
+        raise ValueError("Uniform is prefill-only; decode must use vanilla Sparse")
+    g = kc.shape[1]
+    total_q = int(q.shape[0])
+    max_pages = max(page_count(int(n), block_size) for n in lens)
+    take = min(topk, max_pages)
+    idx = np.full((g, total_q, take), -1, dtype=np.int32)
+    boundary = np.full((g, total_q), np.nan, dtype=np.float32)
+    scores_out = []
+    for b in range(len(lens)):
+        q0, q1 = int(cu_q[b]), int(cu_q[b + 1])
+        c0, c1 = int(cu_c[b]), int(cu_c[b + 1])
+        n = q1 - q0
+        if c1 > c0:
+            atoms = uniform_atom_scores(q[q0:q1], kc[c0:c1], g, policy=policy)
+        else:
+            atoms = np.full((g, n, 1), NEG_INF, dtype=np.float32)
+        sel, bnd, masked = uniform_select_rows(atoms, np.arange(n), seq_len=n, take=take,
+                                               topk=topk, init_blocks=init_blocks,
+                                               local_blocks=local_blocks, block_size=block_size,
+                                               kernel_stride=kernel_stride)
+        idx[:, q0:q1] = sel
+        boundary[:, q0:q1] = bnd
+        scores_out.append((q0, masked))
+    return Selection(idx, boundary, scores_out)
+
+
+def uniform_selection_mismatches(actual: np.ndarray, selection: Selection, *,
+                                 block_size: int = 64, rel_tol: float = 1e-3,
+                                 abs_floor: float = 1e-6, positions=None):
+    """:func:`selection_mismatches` for the uniform method.
+
+    The one difference: a row's pick of page ``q_page + 1`` is dropped from
+    its output, so two selections that differ only by a boundary tie
+    involving that page have different sizes.  Each row's sets are therefore
+    compared after adding that page back to whichever side has one page
+    fewer than the number of picks the row made.  ``positions[t]`` is row
+    ``t``'s position in its sequence (default: from the packed offsets).
+    """
+    expected = selection.topk_idx
+    scores = _score_lookup(selection)
+    bad = []
+    g_count, n, _ = expected.shape
+    for g in range(g_count):
+        for t in range(n):
+            a = set(int(x) for x in actual[g, t] if x >= 0)
+            e = set(int(x) for x in expected[g, t] if x >= 0)
+            if a == e:
+                continue
+            row = scores[(g, t)]
+            if positions is not None:
+                pos = int(positions[t])
+            else:
+                pos = t - max(o for o, _ in selection.page_scores if o <= t)
+            future = pos // block_size + 1
+            width = min(expected.shape[2], row.shape[0])
+            picks = int(np.count_nonzero(~np.isneginf(np.sort(row)[::-1][:width])))
+            if future < row.shape[0]:
+                if len(a) + 1 == picks and future not in a:
+                    a = a | {future}
+                if len(e) + 1 == picks and future not in e:
+                    e = e | {future}
+            bnd = float(selection.boundary[g, t])
+            if len(a) != len(e) or not np.isfinite(bnd):
+                bad.append((g, t, sorted(e - a), sorted(a - e)))
+                continue
+            tol = rel_tol * abs(bnd) + abs_floor
+            if all(abs(float(row[p]) - bnd) <= tol for p in (a ^ e)):
+                continue
+            bad.append((g, t, sorted(e - a), sorted(a - e)))
+    return bad

@@ -211,6 +211,49 @@ def bf16_selection_case():
         kc=kc_ref.float().numpy(), qs=qs, ks=ks, idx=canon(idx))
 
 
+def uniform_cases():
+    """``uniform_prefill_topk_idx`` (ops/uniform.py:185-320) on small packed batches.
+
+    fp32 and bf16 inputs; equal-packed and ragged batches; a sequence too
+    short for any atom; two sinks; no local pages.
+    """
+    from leanselect.ops.uniform import uniform_prefill_topk_idx
+
+    cases = {}
+    specs = [
+        # name, lens, H, G, D, topk, init, local, bf16
+        ("ragged_fp32", [700, 1500, 20, 64], 8, 2, 32, 12, 1, 2, False),
+        ("ragged_bf16", [700, 1500, 20, 64], 8, 2, 32, 12, 1, 2, True),
+        ("equal_bf16_d128", [1024, 1024], 16, 2, 128, 20, 1, 2, True),
+        ("two_sinks", [900], 8, 2, 32, 7, 2, 3, True),
+        ("no_local", [640, 257], 8, 2, 32, 5, 1, 0, True),
+    ]
+    for name, lens, h, g, d, topk, init, local, bf16 in specs:
+        seed = sum(ord(c) for c in name)
+        inputs = ora.synthetic_layer(lens, num_heads=h, num_kv_heads=g, head_dim=d,
+                                     router_heads=4, router_dim=d // 4, hot_pages=3, seed=seed,
+                                     bf16=bf16)
+        dtype = torch.bfloat16 if bf16 else torch.float32
+        kc_t, cu_c_t = CompressK(g, d, kernel_size=32, kernel_stride=16)(
+            torch.from_numpy(inputs.k).to(dtype), torch.from_numpy(inputs.cu_seqlens))
+        with torch.no_grad():
+            idx, _ = uniform_prefill_topk_idx(
+                torch.from_numpy(inputs.q).to(dtype), kc_t,
+                cu_seqlens_q=torch.from_numpy(inputs.cu_seqlens), cu_seqlens_k=cu_c_t,
+                max_seqlen_q=max(lens), topk=topk, block_size=64, kernel_stride=16,
+                init_blocks=init, local_blocks=local)
+        cases[name] = dict(lens=np.array(lens, dtype=np.int64),
+                           dims=np.array([h, g, d], dtype=np.int64), seed=np.int64(seed),
+                           bf16=np.bool_(bf16),
+                           input_digest=np.array(digest(inputs.q, inputs.k, inputs.v)),
+                           kc_digest=np.array(digest(kc_t.float().numpy())),
+                           cu_c=cu_c_t.numpy(), topk=np.int64(topk), init=np.int64(init),
+                           local=np.int64(local), idx=canon(idx.numpy()).astype(np.int16))
+    flat = {f"{name}__{key}": value for name, case in cases.items() for key, value in case.items()}
+    flat["names"] = np.array(list(cases))
+    np.savez_compressed(HERE / "uniform_selection.npz", **flat)
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
     known_answers()
@@ -219,5 +262,6 @@ if __name__ == "__main__":
     selection_cases()
     config0_case()
     bf16_selection_case()
+    uniform_cases()
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)

@@ -420,3 +420,84 @@ def test_nosa_atom_scores_match_oracle():
                                    ora.project_atom_keys(kc[c0:c1], kf, "bf16"))
             np.testing.assert_allclose(rows[..., :c1 - c0], want, rtol=2 ** -7, atol=2e-3)
         assert np.all(np.isneginf(rows[..., c1 - c0:]))
+
+
+# ---------------------------------------------------------------------------
+# Uniform method (ops/uniform.py:185-320)
+# ---------------------------------------------------------------------------
+# The reference's uniform scores are bf16 (its bf16 matmul output, scaled
+# and rounded again).  The GPU accumulates the same products in another
+# order, which can move a score across a bf16 rounding boundary, so pages at
+# the budget boundary may swap within one bf16 ulp: rel_tol = 2**-7.
+
+UNIFORM_CASES = [
+    # lens, H, G, topk, init, local
+    ([700, 1500, 20, 64], 32, 2, 12, 1, 2),
+    ([1024, 1024], 16, 2, 20, 1, 2),
+    ([900], 16, 2, 7, 2, 3),
+    ([640, 257], 32, 2, 5, 1, 0),
+    ([3000, 129], 32, 2, 67, 1, 2),
+]
+
+
+@pytest.mark.parametrize("case", UNIFORM_CASES)
+def test_uniform_select_matches_oracle(case):
+    lens, h, g, topk, init, local = case
+    inp = ora.synthetic_layer(lens, num_heads=h, num_kv_heads=g, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=3, seed=sum(lens) + topk, bf16=True)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    want = ora.uniform_prefill_topk_idx(inp.q, kc, inp.cu_seqlens, cu_c, topk=topk,
+                                        init_blocks=init, local_blocks=local, policy="bf16")
+    got, diag = lsb.uniform_prefill_topk_idx(
+        to_dev(inp.q), to_dev(kc), cu_seqlens_q=cu_dev(inp.cu_seqlens), cu_seqlens_k=cu_dev(cu_c),
+        max_seqlen_q=max(lens), topk=topk, init_blocks=init, local_blocks=local)
+    got = got.cpu().numpy()
+    assert diag.extra["uniform_prefill_head_mix"] == "uniform"
+    assert got.shape == want.topk_idx.shape
+    bad = ora.uniform_selection_mismatches(got, want, rel_tol=2 ** -7)
+    assert not bad, bad[:5]
+    exact = np.mean(np.all(np.sort(got, -1) == np.sort(want.topk_idx, -1), -1))
+    assert exact > 0.97
+    for row in got.reshape(-1, got.shape[-1])[::97]:
+        valid = row[row >= 0]
+        assert np.all(np.diff(valid) > 0) and np.all(row[len(valid):] == -1)
+    assert ops.check_status(DEV) == 0
+
+
+def test_uniform_through_minicpm_dispatch():
+    """``selection_method == "uniform"`` routes the reference call site
+    (minicpm.py:3073-3087) to the uniform kernels."""
+    lens = [1300, 700]
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=3, seed=5, bf16=True)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    module = type("Attn", (), dict(selection_method="uniform", topk=9, block_size=64,
+                                   kernel_stride=16, init_blocks=1, local_blocks=2,
+                                   num_key_value_heads=2, leanselect=None))()
+    q, k, cq, cc = to_dev(inp.q), to_dev(kc), cu_dev(inp.cu_seqlens), cu_dev(cu_c)
+    got = lsb.lightweight_compressed_attention(module, q, k, cq, cc, max(lens))
+    direct, _ = lsb.uniform_prefill_topk_idx(q, k, cu_seqlens_q=cq, cu_seqlens_k=cc,
+                                             max_seqlen_q=max(lens), topk=9, init_blocks=1,
+                                             local_blocks=2)
+    assert torch.equal(got, direct)
+
+
+def test_uniform_config1_rows():
+    """BASELINE config-1 shape (N=32768, 32/2 heads, T=67) on a row sample."""
+    n = 32768
+    inp = ora.synthetic_layer([n], seed=7, bf16=True)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    got, _ = lsb.uniform_prefill_topk_idx(to_dev(inp.q), to_dev(kc),
+                                          cu_seqlens_q=cu_dev(inp.cu_seqlens),
+                                          cu_seqlens_k=cu_dev(cu_c), max_seqlen_q=n, topk=67,
+                                          init_blocks=1, local_blocks=2)
+    got = got.cpu().numpy()
+    rng = np.random.default_rng(3)
+    rows = np.unique(np.concatenate([np.arange(0, 130), np.arange(n - 70, n),
+                                     rng.integers(0, n, 200)]))
+    atoms = ora.uniform_atom_scores(inp.q[rows], kc, 2, policy="bf16")
+    idx, bnd, masked = ora.uniform_select_rows(atoms, rows, seq_len=n, take=67, topk=67,
+                                               init_blocks=1, local_blocks=2)
+    want = ora.Selection(idx, bnd, [(0, masked)])
+    bad = ora.uniform_selection_mismatches(got[:, rows], want, rel_tol=2 ** -7, positions=rows)
+    assert not bad, bad[:5]

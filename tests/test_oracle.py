@@ -265,3 +265,52 @@ def test_row_level_helpers_agree_with_full_oracle():
                                   full.topk_idx, rows=rows)
     got = ora.attention_for_queries(inp.q[rows], rows, inp.k, inp.v, full.topk_idx[:, rows])
     np.testing.assert_allclose(got, out[rows], rtol=1e-6, atol=1e-6)
+
+
+UNIFORM_CASES = ["ragged_fp32", "ragged_bf16", "equal_bf16_d128", "two_sinks", "no_local"]
+
+
+@pytest.mark.parametrize("name", UNIFORM_CASES)
+def test_uniform_selection_matches_reference(name):
+    """The uniform method (ops/uniform.py:185-320) against the reference's own output.
+
+    Exact score ties (adjacent pages sharing a window atom) are the only
+    differences allowed: tolerance 0 beyond ``abs_floor``.
+    """
+    g = load("uniform_selection.npz")
+    h, gq, d = (int(x) for x in g[f"{name}__dims"])
+    bf16 = bool(g[f"{name}__bf16"])
+    lens = g[f"{name}__lens"].tolist()
+    inputs = ora.synthetic_layer(lens, num_heads=h, num_kv_heads=gq, head_dim=d, router_heads=4,
+                                 router_dim=d // 4, hot_pages=3, seed=int(g[f"{name}__seed"]),
+                                 bf16=bf16)
+    assert digest(inputs.q, inputs.k, inputs.v) == str(g[f"{name}__input_digest"])
+    policy = "bf16" if bf16 else "fp32"
+    kc, cu_c = ora.compress_keys(inputs.k, inputs.cu_seqlens, policy=policy)
+    np.testing.assert_array_equal(cu_c, g[f"{name}__cu_c"])
+    sel = ora.uniform_prefill_topk_idx(inputs.q, kc, inputs.cu_seqlens, cu_c,
+                                       topk=int(g[f"{name}__topk"]),
+                                       init_blocks=int(g[f"{name}__init"]),
+                                       local_blocks=int(g[f"{name}__local"]), policy=policy)
+    expected = g[f"{name}__idx"].astype(np.int32)
+    assert sel.topk_idx.shape == expected.shape
+    bad = ora.uniform_selection_mismatches(expected, sel, rel_tol=0.0)
+    assert not bad, bad[:5]
+    # bf16 page scores tie often; the rows that differ differ only by ties.
+    exact = np.mean(np.all(np.sort(sel.topk_idx, -1) == np.sort(expected, -1), -1))
+    assert exact > 0.9
+
+
+def test_uniform_future_page_takes_a_slot():
+    """A query in the last stride of its page sees page q_page+1's first
+    window atom; when that page makes the cut its slot stays -1."""
+    n, g = 512, 1
+    atoms = np.full((g, 1, ora.atom_count(n)), -5.0, dtype=np.float32)
+    atoms[0, 0, 23] = 10.0   # starts at token 368; window atom of pages 5 (19..23) and 6 (23..27)
+    sel, _, masked = ora.uniform_select_rows(atoms, [376], seq_len=n, take=3, topk=3,
+                                             init_blocks=1, local_blocks=0)
+    assert masked[0, 0, 6] == np.float32(10.0)
+    assert sorted(sel[0, 0].tolist()) == [-1, 0, 5]   # sink, local page 5; page 6 dropped
+    sel, _, _ = ora.uniform_select_rows(atoms, [360], seq_len=n, take=3, topk=3,
+                                        init_blocks=1, local_blocks=0)
+    assert sorted(sel[0, 0].tolist()) == [0, 1, 5]    # atom 23 not visible yet at token 360
