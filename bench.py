@@ -237,44 +237,44 @@ def run_ours(args):
         runner.prefill_device(ids_dev, lengths)
     torch.cuda.synchronize()
 
-    # Device-timed region: inputs resident in HBM.
+    # K device-timed steps (inputs resident in HBM, CUDA events on the launching
+    # stream) interleaved with K end-to-end steps through the public call
+    # (pinned host ids -> host logits, wall clock), so that both see the same
+    # clocks; every step is bracketed by a barrier and a synchronize.
     timers = []
     stream = torch.cuda.current_stream(dev)
+    dev_ms, e2e_wall = 0.0, 0.0
     with ClockSampler(local_rank) as clocks:
-        barrier()
-        torch.cuda.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
         for _ in range(args.steps):
+            barrier()
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
             runner.prefill_device(ids_dev, lengths, timers=timers)
-        end.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-    ms_total = start.elapsed_time(end)
+            end.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            dev_ms += start.elapsed_time(end)
+            barrier()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            logits = runner(ids_host, lengths)
+            torch.cuda.synchronize()
+            barrier()
+            e2e_wall += time.perf_counter() - t0
+    ms_total, e2e_total = dev_ms, e2e_wall
     if dist is not None:
-        t = torch.tensor([ms_total], device=dev)
+        t = torch.tensor([ms_total, e2e_total], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total = float(t.item())
+        ms_total, e2e_total = float(t[0].item()), float(t[1].item())
     ms_step = ms_total / args.steps
     value = n / (ms_step / 1e3)
+    e2e_s = e2e_total / args.steps
 
     stage = {"compress": [], "select": [], "attn": []}
     for name, a, b in timers:
         stage[name].append(a.elapsed_time(b))
 
-    # End-to-end through the public call: pinned host ids -> host logits.
-    barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        logits = runner(ids_host, lengths)
-    torch.cuda.synchronize()
-    barrier()
-    e2e_s = (time.perf_counter() - t0) / args.steps
-    if dist is not None:
-        t = torch.tensor([e2e_s], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
     d2h = logits.numel() * logits.element_size() if rank == 0 else 0
 
     pk, pk_kind = peaks()
