@@ -197,6 +197,43 @@ def run_reference(args):
 # GPU arm
 # ---------------------------------------------------------------------------
 
+def gather_roofline(runner, ids_dev, lengths, keys_last_layer: int, reps: int = 3) -> dict:
+    """The attention kernel against its own data movement (measured roofline).
+
+    Re-runs the last layer's attention call on the bench's own inputs next to
+    ``ls_sparse_attn_gather_only``, which moves the same K/V pages from L2
+    into shared memory with the same grid and TMA ring but does no math: the
+    ratio is how close the kernel runs to the gather bound it cannot beat.
+    Untimed by the bench's step clock (after the timed region).
+    """
+    from leanselect_b200 import ops
+
+    cap = {}
+    runner.prefill_device(ids_dev, lengths, capture=cap)
+    q, k, v, idx, cu, max_len = (cap[x] for x in ("q", "k", "v", "idx", "cu", "max_len"))
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    attn_ms = timed(lambda: ops.sparse_attn(q, k, v, cu, cu, max_len, max_len, idx))
+    gather_ms = timed(lambda: ops.sparse_attn_gather_only(q, k, v, cu, cu, max_len, max_len, idx))
+    ops.check_status(q.device)
+    gathered = keys_last_layer * 2 * q.shape[-1] * q.element_size()  # K and V rows
+    return {"gathered_bytes": gathered, "attn_ms": attn_ms, "gather_only_ms": gather_ms,
+            "achieved_tbs": gathered / (attn_ms / 1e3) / 1e12,
+            "ceiling_tbs": gathered / (gather_ms / 1e3) / 1e12,
+            "frac": gather_ms / attn_ms,
+            "note": "L2 -> shared-memory page gather; ceiling = same launch with the math removed"}
+
+
 def run_ours(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -327,10 +364,15 @@ def run_ours(args):
             "frac": achieved / peak,
             "peak_kind": f"{pk_kind} (bf16 dense, sustained)",
             "flops_per_launch": flops_per_launch,
-            "traffic": None,
+            # dram__bytes_read.sum + dram__bytes_write.sum per attention launch of
+            # this command at 131072 tokens, mean of 24 launches in one ncu pass
+            # (profiles/bench_128k_4layer_launch_list.md).
+            "traffic": 6858.6e6 + 1071.0e6,
         },
         "clocks": clocks.summary(),
     }
+    if world == 1:
+        line["roofline"]["l2_gather"] = gather_roofline(runner, ids_dev, lengths, key_counts[-1])
     if rank == 0 and world == 1:
         cpu = CpuHotPath(n, args.layers, args.cpu_rows, args.seed)
         line["cpu_baseline"] = cpu.describe(cpu.step())

@@ -277,6 +277,22 @@ int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                    float softmax_scale, int32_t causal, uint16_t* out, float* lse,
                    int32_t* status, void* stream);
 
+/*
+ * ls_sparse_attn_gather_only -- measurement twin of ls_sparse_attn (no
+ * reference counterpart).  Runs the same grid over the same page lists and
+ * moves the same K/V pages from L2 into shared memory through the same TMA
+ * ring, but computes and writes nothing: its duration is the gather time
+ * that bounds ls_sparse_attn on the caller's inputs (the kernel's measured
+ * roofline).  Arguments as ls_sparse_attn without scale and outputs.
+ */
+int ls_sparse_attn_gather_only(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                               const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                               int32_t batch, int32_t max_seqlen_q, int32_t max_seqlen_k,
+                               int64_t total_q, int64_t total_k, int32_t num_heads,
+                               int32_t num_kv_heads, int32_t head_dim, const int32_t* topk_idx,
+                               int32_t topk, int32_t block_size, int32_t causal, int32_t* status,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -467,14 +467,17 @@ int ls_select_pages_chunk(const uint16_t* q, const uint16_t* wq_t, const uint16_
   return err == cudaSuccess ? LS_OK : cuda_fail(err, "select_pages_chunk launch");
 }
 
-int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
-                   const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t batch,
-                   int32_t max_seqlen_q, int32_t max_seqlen_k, int64_t total_q, int64_t total_k,
-                   int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
-                   const int32_t* topk_idx, int32_t topk, int32_t block_size,
-                   float softmax_scale, int32_t causal, uint16_t* out, float* lse,
-                   int32_t* status, void* stream) {
-  LS_REQUIRE(q && k && v && cu_seqlens_q && cu_seqlens_k && out, "null argument");
+namespace {
+
+int sparse_attn_impl(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                     const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t batch,
+                     int32_t max_seqlen_q, int32_t max_seqlen_k, int64_t total_q, int64_t total_k,
+                     int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                     const int32_t* topk_idx, int32_t topk, int32_t block_size,
+                     float softmax_scale, int32_t causal, uint16_t* out, float* lse,
+                     int32_t* status, void* stream, bool gather_only) {
+  LS_REQUIRE(q && k && v && cu_seqlens_q && cu_seqlens_k && (out || gather_only),
+             "null argument");
   LS_REQUIRE(batch >= 1 && total_q >= 0 && total_k >= 0, "bad sizes");
   LS_REQUIRE(total_q < (int64_t{1} << 31) && total_k < (int64_t{1} << 31), "totals out of range");
   LS_REQUIRE(max_seqlen_q >= 0 && max_seqlen_k >= 0, "bad max_seqlen");
@@ -490,7 +493,7 @@ int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
   LS_REQUIRE_ALIGNED(q);
   LS_REQUIRE_ALIGNED(k);
   LS_REQUIRE_ALIGNED(v);
-  LS_REQUIRE_ALIGNED(out);
+  if (out) LS_REQUIRE_ALIGNED(out);
   if (total_q == 0) return LS_OK;
   AttnArgs a{};
   const uint64_t row = static_cast<uint64_t>(num_kv_heads) * 128;
@@ -517,8 +520,36 @@ int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
   a.lse = lse;
   a.status = status;
   a.order = 1;  // group-major: resident CTAs share one group's K/V in L2
-  const cudaError_t err = launch_sparse_attn(a, static_cast<cudaStream_t>(stream));
+  const cudaError_t err = gather_only
+                              ? launch_sparse_attn_gather_only(a, static_cast<cudaStream_t>(stream))
+                              : launch_sparse_attn(a, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? LS_OK : cuda_fail(err, "sparse_attn launch");
+}
+
+}  // namespace
+
+int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                   const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t batch,
+                   int32_t max_seqlen_q, int32_t max_seqlen_k, int64_t total_q, int64_t total_k,
+                   int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                   const int32_t* topk_idx, int32_t topk, int32_t block_size,
+                   float softmax_scale, int32_t causal, uint16_t* out, float* lse,
+                   int32_t* status, void* stream) {
+  return sparse_attn_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, batch, max_seqlen_q, max_seqlen_k,
+                          total_q, total_k, num_heads, num_kv_heads, head_dim, topk_idx, topk,
+                          block_size, softmax_scale, causal, out, lse, status, stream, false);
+}
+
+int ls_sparse_attn_gather_only(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                               const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                               int32_t batch, int32_t max_seqlen_q, int32_t max_seqlen_k,
+                               int64_t total_q, int64_t total_k, int32_t num_heads,
+                               int32_t num_kv_heads, int32_t head_dim, const int32_t* topk_idx,
+                               int32_t topk, int32_t block_size, int32_t causal, int32_t* status,
+                               void* stream) {
+  return sparse_attn_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, batch, max_seqlen_q, max_seqlen_k,
+                          total_q, total_k, num_heads, num_kv_heads, head_dim, topk_idx, topk,
+                          block_size, 0.f, causal, nullptr, nullptr, status, stream, true);
 }
 
 }  // extern "C"

@@ -97,6 +97,12 @@ struct AttnArgs {
 
 cudaError_t launch_sparse_attn(const AttnArgs& args, cudaStream_t stream);
 
+// The attention launch's data movement alone: same grid, page lists, TMA
+// boxes and shared-memory ring, consumers release each stage unread and
+// nothing is written.  Its duration is the L2 -> shared-memory gather time
+// the attention kernel cannot beat (a measured roofline for it).
+cudaError_t launch_sparse_attn_gather_only(const AttnArgs& args, cudaStream_t stream);
+
 // Records `message` as the calling thread's ls_last_error() text; returns `code`.
 int set_host_error(int code, const char* message);
 

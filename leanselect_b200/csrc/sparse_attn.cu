@@ -109,7 +109,7 @@ __device__ __forceinline__ void warp_bitonic_sort128(int32_t (&v)[4], int lane) 
   }
 }
 
-template <int HG>
+template <int HG, bool kGatherOnly>
 __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_constant__ AttnArgs args) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -211,6 +211,15 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
   }
 
   // ------------------------------------------------------------------ consumers
+  if constexpr (kGatherOnly) {
+    for (int i = 0; i < n_pages; ++i) {
+      const int s = i % kStages;
+      if (!mbar_wait(&sm->full[s], (i / kStages) & 1, args.status, abort_flag)) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm->empty[s]);
+    }
+    return;
+  }
   // Q fragments for the 8 k-steps (rows = heads, k = dims).
   uint32_t qa[8][4];
   {
@@ -424,26 +433,35 @@ size_t attn_smem_bytes() { return 1024 + kStages * kStageBytes + 16 * 256 + size
 
 }  // namespace
 
-cudaError_t launch_sparse_attn(const AttnArgs& args, cudaStream_t stream) {
+template <bool kGatherOnly>
+cudaError_t launch_attn(const AttnArgs& args, cudaStream_t stream) {
   const int64_t grid = args.total_q * args.num_groups;
   if (grid == 0) return cudaSuccess;
   const size_t smem = attn_smem_bytes();
   const int hg = args.num_heads / args.num_groups;
   cudaError_t err;
   if (hg == 16) {
-    err = cudaFuncSetAttribute(sparse_attn_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(smem));
+    err = cudaFuncSetAttribute(sparse_attn_kernel<16, kGatherOnly>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (err != cudaSuccess) return err;
-    sparse_attn_kernel<16><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
+    sparse_attn_kernel<16, kGatherOnly><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
   } else if (hg == 8) {
-    err = cudaFuncSetAttribute(sparse_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(smem));
+    err = cudaFuncSetAttribute(sparse_attn_kernel<8, kGatherOnly>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (err != cudaSuccess) return err;
-    sparse_attn_kernel<8><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
+    sparse_attn_kernel<8, kGatherOnly><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
   } else {
     return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+
+cudaError_t launch_sparse_attn(const AttnArgs& args, cudaStream_t stream) {
+  return launch_attn<false>(args, stream);
+}
+
+cudaError_t launch_sparse_attn_gather_only(const AttnArgs& args, cudaStream_t stream) {
+  return launch_attn<true>(args, stream);
 }
 
 }  // namespace ls

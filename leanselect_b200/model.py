@@ -189,12 +189,14 @@ class PrefillModel:
 
     def prefill(self, input_ids: torch.Tensor, cu_seqlens: torch.Tensor,
                 lengths: Sequence[int], timers: list | None = None,
-                key_counts: list | None = None) -> torch.Tensor:
+                key_counts: list | None = None, capture: dict | None = None) -> torch.Tensor:
         """Packed prefill of ``len(lengths)`` sequences; returns ``[B, vocab]`` fp32 logits.
 
         ``timers`` (optional) collects per-layer hot-path stage events (see
         ``prefill_layer_attention``); ``key_counts`` (optional, adds host
-        syncs) collects each layer's attended-key count.
+        syncs) collects each layer's attended-key count; ``capture``
+        (optional dict) receives the last layer's attention inputs
+        (``q``, ``k``, ``v``, ``idx``, ``cu``, ``max_len``) for profiling.
         """
         s = self.shape
         lengths = [int(n) for n in lengths]
@@ -209,6 +211,8 @@ class PrefillModel:
                                                 timers=timers)
             if key_counts is not None:
                 key_counts.append(count_attended_keys(idx, lengths, s.sparse.block_size))
+            if capture is not None and layer is self.layers[-1]:
+                capture.update(q=q, k=k, v=v, idx=idx, cu=cu_seqlens, max_len=max_len)
             del q, k, v, idx
             h.addmm_(attn.view(h.shape[0], -1), layer.w_o.t(), alpha=self.residual_scale)
             del attn

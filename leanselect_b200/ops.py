@@ -394,3 +394,26 @@ def sparse_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q:
     if q.dtype != torch.bfloat16:
         out = out.to(q.dtype)
     return (out, lse) if return_lse else out
+
+
+def sparse_attn_gather_only(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                            cu_seqlens_q: torch.Tensor, cu_seqlens_k: torch.Tensor,
+                            max_seqlen_q: int, max_seqlen_k: int, topk_idx: torch.Tensor, *,
+                            causal: bool = True, block_size: int = 64) -> None:
+    """The data movement of :func:`sparse_attn` alone (measured gather roofline).
+
+    Same launch geometry, page lists and TMA ring; no math, no output.  Its
+    duration is the L2 -> shared-memory gather time of that attention call.
+    """
+    dev = _require_cuda(q, k, v, cu_seqlens_q, cu_seqlens_k, topk_idx)
+    qb, kb, vb = _bf16(q), _bf16(k), _bf16(v)
+    total_q, H, D = qb.shape
+    total_k, G, _ = kb.shape
+    idx = _i32(topk_idx)
+    if idx.ndim != 3 or idx.shape[0] != G or idx.shape[1] != total_q:
+        raise ValueError("topk_idx must be [num_kv_heads, total_q, T]")
+    cu_q, cu_k = _i32(cu_seqlens_q), _i32(cu_seqlens_k)
+    _native.call("ls_sparse_attn_gather_only", qb.data_ptr(), kb.data_ptr(), vb.data_ptr(),
+                 cu_q.data_ptr(), cu_k.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q),
+                 int(max_seqlen_k), total_q, total_k, H, G, D, idx.data_ptr(), idx.shape[2],
+                 block_size, 1 if causal else 0, status_word(dev).data_ptr(), _stream(dev))

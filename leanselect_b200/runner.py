@@ -21,13 +21,14 @@ class PrefillRunner:
         self.model = model if model is not None else PrefillModel(shape, self.device, seed=seed)
 
     def prefill_device(self, ids: torch.Tensor, lengths: Sequence[int], timers=None,
-                       key_counts=None):
+                       key_counts=None, capture=None):
         """Prefill with ids already on the device; returns device logits ``[B, vocab]``."""
         lengths = [int(n) for n in lengths]
         cu = torch.zeros(len(lengths) + 1, dtype=torch.int32)
         cu[1:] = torch.tensor(lengths).cumsum(0)
         cu = cu.to(self.device, non_blocking=True)
-        return self.model.prefill(ids, cu, lengths, timers=timers, key_counts=key_counts)
+        return self.model.prefill(ids, cu, lengths, timers=timers, key_counts=key_counts,
+                                  capture=capture)
 
     def __call__(self, ids_host: torch.Tensor, lengths: Sequence[int]) -> torch.Tensor:
         """Host ids (ideally pinned) -> host logits ``[B, vocab]`` fp32."""
