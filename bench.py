@@ -365,8 +365,9 @@ def run_ours(args):
             "peak_kind": f"{pk_kind} (bf16 dense, sustained)",
             "flops_per_launch": flops_per_launch,
             # dram__bytes_read.sum + dram__bytes_write.sum per attention launch of
-            # this command at 131072 tokens, mean of 24 launches in one ncu pass
-            # (profiles/bench_128k_4layer_launch_list.md).
+            # this command at 131072 tokens: mean of 24 launches captured in one
+            # ncu pass (`--metrics gpu__time_duration.sum,dram__bytes_read.sum,
+            # dram__bytes_write.sum`, 4 layers).
             "traffic": 6858.6e6 + 1071.0e6,
         },
         "clocks": clocks.summary(),
