@@ -78,6 +78,83 @@ def lpt_shards(lengths: Sequence[int], world: int) -> list[list[int]]:
     return [sorted(s) for s in shards]
 
 
+_CU_CACHE: dict[tuple, torch.Tensor] = {}
+
+
+def sequence_parallel_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_len: int,
+                            selector, cfg, group=None, timers: list | None = None,
+                            key_counts: list | None = None) -> torch.Tensor:
+    """The hot path of one layer for this rank's two zig-zag query chunks.
+
+    ``q [2C, H, D]``, ``k``/``v [2C, G, D]`` are this rank's rows (chunk ``r``
+    then chunk ``2W-1-r``, post-RoPE).  All-gathers K/V into the whole
+    sequence, compresses it, projects the atom keys, selects pages for the
+    local query rows at their true positions and runs the sparse attention
+    over each chunk's causal key prefix.  Returns the local attention output
+    ``[2C, H, D]``.  ``timers`` receives ``(stage, start, end)`` CUDA events
+    for "gather", "compress", "select" and "attn".
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    n = int(seq_len)
+    chunks = zigzag_chunks(n, world, rank)
+    c = chunks[0][1]
+    g, d = k.shape[1], k.shape[2]
+    dev = q.device
+
+    def mark():
+        if timers is None:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return ev
+
+    def cu(*values):
+        key = (str(dev),) + values
+        t = _CU_CACHE.get(key)
+        if t is None:
+            t = _CU_CACHE[key] = torch.tensor(values, dtype=torch.int32, device=dev)
+        return t
+
+    e_g = mark()
+    kv = torch.stack((k.reshape(2 * c, -1), v.reshape(2 * c, -1)), dim=1)
+    full = gather_sequence(kv, n, group)                 # [n, 2, G*D]
+    k_full = full[:, 0].reshape(n, g, d).contiguous()
+    v_full = full[:, 1].reshape(n, g, d).contiguous()
+    del kv, full
+    e0 = mark()
+    kc, _ = ops.compress_keys(k_full, cu(0, n), kernel_size=cfg.kernel_size,
+                              kernel_stride=cfg.kernel_stride, lengths=[n])
+    e1 = mark()
+    pages = (n + cfg.block_size - 1) // cfg.block_size
+    take = min(cfg.topk, pages)
+    weights = selector.kernel_weights()
+    ks = ops.project_atom_keys(kc, weights.wk_t)
+    idxs = []
+    for i, (start, length) in enumerate(chunks):
+        idxs.append(ops.select_pages_chunk(
+            q[i * c:(i + 1) * c], weights, ks, q_position=start, seq_len=n, take=take,
+            init_blocks=cfg.init_blocks, local_blocks=cfg.local_blocks,
+            block_size=cfg.block_size, kernel_stride=cfg.kernel_stride))
+    e2 = mark()
+    attn = torch.empty_like(q)
+    for i, (start, length) in enumerate(chunks):
+        ops.sparse_attn(q[i * c:(i + 1) * c], k_full, v_full, cu(0, length), cu(0, start + length),
+                        length, start + length, idxs[i], causal=True, out=attn[i * c:(i + 1) * c])
+    e3 = mark()
+    if timers is not None:
+        timers.extend([("gather", e_g, e0), ("compress", e0, e1), ("select", e1, e2),
+                       ("attn", e2, e3)])
+    if key_counts is not None:
+        positions = local_positions(n, world, rank, device=dev)
+        total = 0
+        for i, (start, length) in enumerate(chunks):
+            total += count_attended_keys(idxs[i], None, cfg.block_size,
+                                         positions=positions[i * c:(i + 1) * c])
+        key_counts.append(total)
+    return attn
+
+
 class DataParallelRunner:
     """Batched prefill: sequences sharded over ranks, no collectives.
 
@@ -143,56 +220,17 @@ class SequenceParallelRunner:
         positions = local_positions(n, self.world, self.rank, device=self.device)
         freqs = m.rope.frequencies(n)
         h = m.embed[local_ids] * s.scale_emb
-        cu_full = self._cu(0, n)
-        cfg = s.sparse
-        pages = (n + cfg.block_size - 1) // cfg.block_size
-        take = min(cfg.topk, pages)
-
-        def mark():
-            if timers is None:
-                return None
-            ev = torch.cuda.Event(enable_timing=True)
-            ev.record()
-            return ev
-
+        layer_timers = [] if timers is not None else None
         for layer in m.layers:
             q, k, v = m.qkv(layer, h, positions, freqs)
-            kv = torch.stack((k.reshape(2 * c, -1), v.reshape(2 * c, -1)), dim=1)
-            full = gather_sequence(kv, n, self.group)           # [n, 2, G*D]
-            k_full = full[:, 0].reshape(n, s.num_kv_heads, s.head_dim).contiguous()
-            v_full = full[:, 1].reshape(n, s.num_kv_heads, s.head_dim).contiguous()
-            del kv, full, k, v
-            e0 = mark()
-            kc, _ = ops.compress_keys(k_full, cu_full, kernel_size=cfg.kernel_size,
-                                      kernel_stride=cfg.kernel_stride, lengths=[n])
-            e1 = mark()
-            weights = layer.selector.kernel_weights()
-            ks = ops.project_atom_keys(kc, weights.wk_t)
-            idxs = []
-            for i, (start, length) in enumerate(chunks):
-                idxs.append(ops.select_pages_chunk(
-                    q[i * c:(i + 1) * c], weights, ks, q_position=start, seq_len=n, take=take,
-                    init_blocks=cfg.init_blocks, local_blocks=cfg.local_blocks,
-                    block_size=cfg.block_size, kernel_stride=cfg.kernel_stride))
-            e2 = mark()
-            attn = torch.empty_like(q)
-            for i, (start, length) in enumerate(chunks):
-                ops.sparse_attn(q[i * c:(i + 1) * c], k_full, v_full, self._cu(0, length),
-                                self._cu(0, start + length), length, start + length, idxs[i],
-                                causal=True, out=attn[i * c:(i + 1) * c])
-            e3 = mark()
-            if timers is not None:
-                timers.extend([("compress", e0, e1), ("select", e1, e2), ("attn", e2, e3)])
-            if key_counts is not None:
-                total = 0
-                for i, (start, length) in enumerate(chunks):
-                    total += count_attended_keys(idxs[i], None, cfg.block_size,
-                                                 positions=positions[i * c:(i + 1) * c])
-                key_counts.append(total)
-            del q, k_full, v_full, kc, ks, idxs
+            attn = sequence_parallel_layer(q, k, v, n, layer.selector, s.sparse, self.group,
+                                           timers=layer_timers, key_counts=key_counts)
+            del q, k, v
             h.addmm_(attn.view(h.shape[0], -1), layer.w_o.t(), alpha=m.residual_scale)
             del attn
             m.mlp_residual(layer, h)
+        if timers is not None:
+            timers.extend(t for t in layer_timers if t[0] != "gather")
         if self.rank == 0:
             return m.logits(h[-1:])
         return None
