@@ -444,6 +444,8 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
 // ---------------------------------------------------------------------------
 
 constexpr int kTopkWarps = 8;
+constexpr int kDirectMax = 256;      // rows with at most this many candidates: radix on the row
+constexpr int kBufCap = 512;         // per-warp candidate buffer of the filtered path
 
 // Order-preserving map of fp32 to uint32; -inf and NaN map to 0 (never picked).
 __device__ __forceinline__ uint32_t score_key(float s) {
@@ -452,11 +454,131 @@ __device__ __forceinline__ uint32_t score_key(float s) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+struct RowKeys {          // candidate i of a workspace row
+  const float* p;
+  __device__ __forceinline__ uint32_t operator()(int i) const { return score_key(p[i]); }
+};
+struct BufKeys {          // entry j of the warp's filtered buffer
+  const uint32_t* k;
+  __device__ __forceinline__ uint32_t operator()(int j) const { return k[j]; }
+};
+
+// Exact threshold of the `need` largest nonzero keys among keys(0 .. count-1):
+// MSB-first radix select, 4 passes of 8 bits over warp histograms in shared
+// memory.  Returns the threshold key; `need` becomes the number of keys equal
+// to it that belong to the selection (the lowest indices win).
+template <class Keys>
+__device__ uint32_t radix_threshold(const Keys& keys, int count, int& need, uint32_t* hist,
+                                    int lane) {
+  uint32_t prefix = 0, mask = 0;
+#pragma unroll 1
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int k = lane; k < 256; k += 32) hist[k] = 0;
+    __syncwarp();
+    for (int i = lane; i < count; i += 32) {
+      const uint32_t key = keys(i);
+      if (key != 0u && ((key ^ prefix) & mask) == 0) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncwarp();
+    // Lane l owns bins 255-8l .. 248-8l (descending).
+    uint32_t c[8];
+    uint32_t lane_sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      c[j] = hist[255 - 8 * lane - j];
+      lane_sum += c[j];
+    }
+    uint32_t incl = lane_sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const uint32_t excl = incl - lane_sum;
+    const bool here = excl < static_cast<uint32_t>(need) && incl >= static_cast<uint32_t>(need);
+    const uint32_t owner_mask = __ballot_sync(0xffffffffu, here);
+    const int owner = __ffs(owner_mask) - 1;
+    int bin = 0;
+    uint32_t above = 0;
+    if (here) {
+      uint32_t cum = excl;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (cum + c[j] >= static_cast<uint32_t>(need)) {
+          bin = 255 - 8 * lane - j;
+          above = cum;
+          break;
+        }
+        cum += c[j];
+      }
+    }
+    bin = __shfl_sync(0xffffffffu, bin, owner);
+    above = __shfl_sync(0xffffffffu, above, owner);
+    need -= static_cast<int>(above);
+    prefix |= static_cast<uint32_t>(bin) << shift;
+    mask |= 0xFFu << shift;
+    __syncwarp();
+  }
+  return prefix;
+}
+
+// Writes, in index order, the candidates among keys(0 .. count-1) that are
+// above `thr` plus the first `ties` equal to it (all nonzero keys when
+// `all`), as page numbers `index(j) + base`; candidate `skip` is selected but
+// not written.  Returns the next output position.
+template <class Keys, class Index>
+__device__ int emit_selected(const Keys& keys, const Index& index, int count, bool all,
+                             uint32_t thr, int ties, int skip, int base, int32_t* out, int k_out,
+                             int lane) {
+  int ties_seen = 0;
+  for (int b0 = 0; b0 < count; b0 += 32) {
+    const int j = b0 + lane;
+    const uint32_t key = j < count ? keys(j) : 0u;
+    bool take;
+    if (all) {
+      take = key != 0u;
+    } else {
+      const bool tie = key == thr && key != 0u;
+      const uint32_t tie_mask = __ballot_sync(0xffffffffu, tie);
+      const int tie_rank = ties_seen + __popc(tie_mask & ((1u << lane) - 1));
+      take = key > thr || (tie && tie_rank < ties);
+      ties_seen += __popc(tie_mask);
+    }
+    const int i = j < count ? index(j) : -1;
+    if (i == skip) take = false;  // the slot page qp+1 won stays empty
+    const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
+    if (take) out[k_out + __popc(take_mask & ((1u << lane) - 1))] = base + i;
+    k_out += __popc(take_mask);
+  }
+  return k_out;
+}
+
+struct Identity {
+  __device__ __forceinline__ int operator()(int j) const { return j; }
+};
+struct BufIndex {
+  const int32_t* idx;
+  __device__ __forceinline__ int operator()(int j) const { return idx[j]; }
+};
+
+// Top-T' of each (group, query) row.  Rows with more than kDirectMax
+// candidates first estimate a cut from a 1/8 sample (every 8th group of 32
+// consecutive candidates, linear histogram between the sample's min and max,
+// aiming at ~1.5x the needed count), then keep the candidates at or above it
+// in a shared-memory buffer in one pass and select exactly among those.
+// The exact radix over the whole row runs for short rows and whenever the
+// estimate kept too few or too many candidates.  The result is identical
+// either way.
 __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_constant__ ScoreArgs args) {
   __shared__ uint32_t hist_all[kTopkWarps][256];
+  __shared__ uint32_t buf_key_all[kTopkWarps][kBufCap];
+  __shared__ int32_t buf_idx_all[kTopkWarps][kBufCap];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   uint32_t* hist = hist_all[warp];
+  uint32_t* buf_key = buf_key_all[warp];
+  int32_t* buf_idx = buf_idx_all[warp];
   const int64_t rows_total = static_cast<int64_t>(args.num_groups) * args.total_q;
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * kTopkWarps + warp; r < rows_total;
        r += static_cast<int64_t>(gridDim.x) * kTopkWarps) {
@@ -511,91 +633,133 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
     // the score kernel in slot n_init + m, the first non-sink local page.
     const int sinks_out = min(n_init, take_b);
     for (int k = lane; k < sinks_out; k += 32) out[k] = k;
+    const float* cand = scores + n_init;
+    const RowKeys row_keys{cand};
+    int k_out = sinks_out;
 
-    // ---- threshold key by MSB-first radix select over the candidates.
-    uint32_t prefix = 0, mask = 0;
-    int need = cap;
-    int valid_total = 0;
     if (cap > 0) {
-      // Count finite candidates first: if all fit, no selection is needed.
-      for (int i = lane; i < m_all; i += 32) valid_total += score_key(scores[n_init + i]) != 0u;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) valid_total += __shfl_xor_sync(0xffffffffu, valid_total, o);
-    }
-    const bool select_all = valid_total <= cap;
-    if (cap > 0 && !select_all) {
-#pragma unroll 1
-      for (int pass = 0; pass < 4; ++pass) {
-        const int shift = 24 - 8 * pass;
-        for (int k = lane; k < 256; k += 32) hist[k] = 0;
-        __syncwarp();
-        for (int i = lane; i < m_all; i += 32) {
-          const uint32_t key = score_key(scores[n_init + i]);
-          if (key != 0u && ((key ^ prefix) & mask) == 0) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-        }
-        __syncwarp();
-        // Lane l owns bins 255-8l .. 248-8l (descending).
-        uint32_t c[8];
-        uint32_t lane_sum = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          c[j] = hist[255 - 8 * lane - j];
-          lane_sum += c[j];
-        }
-        uint32_t incl = lane_sum;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += t;
-        }
-        const uint32_t excl = incl - lane_sum;
-        const bool here = excl < static_cast<uint32_t>(need) && incl >= static_cast<uint32_t>(need);
-        const uint32_t owner_mask = __ballot_sync(0xffffffffu, here);
-        const int owner = __ffs(owner_mask) - 1;
-        int bin = 0;
-        uint32_t above = 0;
-        if (here) {
-          uint32_t cum = excl;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            if (cum + c[j] >= static_cast<uint32_t>(need)) {
-              bin = 255 - 8 * lane - j;
-              above = cum;
-              break;
+      bool done = false;
+      if (m_all > kDirectMax) {
+        // ---- 1/8 sample: min, max and count of the finite sampled scores.
+        float smin = INFINITY, smax = -INFINITY;
+        int fs = 0, sampled = 0;
+        for (int b0 = 0; b0 < m_all; b0 += 256) {
+          const int i = b0 + lane;
+          sampled += min(32, m_all - b0);
+          if (i < m_all) {
+            const float v = cand[i];
+            if (v > -INFINITY) {
+              ++fs;
+              smin = fminf(smin, v);
+              smax = fmaxf(smax, v);
             }
-            cum += c[j];
           }
         }
-        bin = __shfl_sync(0xffffffffu, bin, owner);
-        above = __shfl_sync(0xffffffffu, above, owner);
-        need -= static_cast<int>(above);
-        prefix |= static_cast<uint32_t>(bin) << shift;
-        mask |= 0xFFu << shift;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          fs += __shfl_xor_sync(0xffffffffu, fs, o);
+          smin = fminf(smin, __shfl_xor_sync(0xffffffffu, smin, o));
+          smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
+        }
+        uint32_t cut = 1u;  // keep every finite key unless the sample says better
+        if (fs > 0 && smax > smin) {
+          // Linear 128-bin histogram of the sample; the cut is the lower edge of
+          // the bin where the count from the top reaches ~1.5 cap * sampled/m_all.
+          const float scale = 128.f / (smax - smin);
+          for (int k = lane; k < 128; k += 32) hist[k] = 0;
+          __syncwarp();
+          for (int b0 = 0; b0 < m_all; b0 += 256) {
+            const int i = b0 + lane;
+            if (i < m_all) {
+              const float v = cand[i];
+              if (v > -INFINITY) atomicAdd(&hist[min(127, static_cast<int>((v - smin) * scale))], 1u);
+            }
+          }
+          __syncwarp();
+          const int target = max(1, min(fs, static_cast<int>(1.5f * cap * sampled / m_all) + 1));
+          uint32_t c4[4];
+          uint32_t lane_sum = 0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            c4[j] = hist[127 - 4 * lane - j];
+            lane_sum += c4[j];
+          }
+          uint32_t incl = lane_sum;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+          }
+          const uint32_t excl = incl - lane_sum;
+          const bool here = excl < static_cast<uint32_t>(target) && incl >= static_cast<uint32_t>(target);
+          const uint32_t owner_mask = __ballot_sync(0xffffffffu, here);
+          int bin = 0;
+          if (here) {
+            uint32_t cum = excl;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              cum += c4[j];
+              if (cum >= static_cast<uint32_t>(target)) {
+                bin = 127 - 4 * lane - j;
+                break;
+              }
+            }
+          }
+          if (owner_mask != 0u) {
+            bin = __shfl_sync(0xffffffffu, bin, __ffs(owner_mask) - 1);
+            cut = max(1u, score_key(smin + static_cast<float>(bin) / scale));
+          }
+          __syncwarp();
+        }
+        // ---- one pass: count finite candidates, keep those at or above the cut.
+        int kept = 0, finite = 0;
+        bool overflow = false;
+        for (int b0 = 0; b0 < m_all; b0 += 32) {
+          const int i = b0 + lane;
+          const uint32_t key = i < m_all ? row_keys(i) : 0u;
+          finite += __popc(__ballot_sync(0xffffffffu, key != 0u));
+          const bool keep = key >= cut && key != 0u;
+          const uint32_t keep_mask = __ballot_sync(0xffffffffu, keep);
+          const int nk = __popc(keep_mask);
+          if (!overflow) {
+            if (kept + nk > kBufCap) {
+              overflow = true;
+            } else {
+              if (keep) {
+                const int at = kept + __popc(keep_mask & ((1u << lane) - 1));
+                buf_key[at] = key;
+                buf_idx[at] = i;
+              }
+              kept += nk;
+            }
+          }
+        }
+        __syncwarp();
+        if (finite <= cap) {
+          k_out = emit_selected(row_keys, Identity{}, m_all, true, 0u, 0, future, n_init, out, k_out,
+                                lane);
+          done = true;
+        } else if (!overflow && kept >= cap) {
+          const BufKeys bk{buf_key};
+          int need = cap;
+          const uint32_t thr = radix_threshold(bk, kept, need, hist, lane);
+          k_out = emit_selected(bk, BufIndex{buf_idx}, kept, false, thr, need, future, n_init, out,
+                                k_out, lane);
+          done = true;
+        }
         __syncwarp();
       }
-    }
-    // ---- emit candidates in page order: keys above the threshold, plus the
-    // first `need` keys equal to it (lower pages first).
-    int k_out = sinks_out;
-    if (cap > 0) {
-      int ties_seen = 0;
-      for (int base = 0; base < m_all; base += 32) {
-        const int i = base + lane;
-        const uint32_t key = i < m_all ? score_key(scores[n_init + i]) : 0u;
-        bool take;
-        if (select_all) {
-          take = key != 0u;
-        } else {
-          const bool tie = key == prefix;
-          const uint32_t tie_mask = __ballot_sync(0xffffffffu, tie);
-          const int tie_rank = ties_seen + __popc(tie_mask & ((1u << lane) - 1));
-          take = key > prefix || (tie && tie_rank < need);
-          ties_seen += __popc(tie_mask);
-        }
-        if (i == future) take = false;  // the slot page qp+1 won stays empty
-        const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
-        if (take) out[k_out + __popc(take_mask & ((1u << lane) - 1))] = n_init + i;
-        k_out += __popc(take_mask);
+      if (!done) {
+        // ---- exact radix over the whole row.
+        int finite = 0;
+        for (int i = lane; i < m_all; i += 32) finite += row_keys(i) != 0u;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) finite += __shfl_xor_sync(0xffffffffu, finite, o);
+        const bool all = finite <= cap;
+        int need = cap;
+        const uint32_t thr = all ? 0u : radix_threshold(row_keys, m_all, need, hist, lane);
+        k_out = emit_selected(row_keys, Identity{}, m_all, all, thr, need, future, n_init, out, k_out,
+                              lane);
       }
     }
     // Local pages (those that are not sinks), then padding.

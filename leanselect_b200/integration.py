@@ -40,12 +40,18 @@ def install_module_symbols(module) -> None:
 
     ``load_model`` requires ``infllmv2_attn_stage1``, ``infllmv2_attn_varlen_func``
     and ``max_pooling_1d_varlen`` to be callable (models/__init__.py:69-85) and
-    ``sparse_forward`` calls the module-level ``infllmv2_attn_varlen_func``.
-    Only the LeanSelect method is served; the other two raise if called.
+    ``sparse_forward`` calls the module-level ``infllmv2_attn_varlen_func`` for
+    prefill and decode alike.  The attention is always the B200 kernel.  The
+    native InfLLM-v2 stage-1 selection (used by the reference for decode and
+    for the native method) is not part of this library: the module's own
+    functions are kept when the extension provided them, and stubs that raise
+    are bound only where they are missing.
     """
     module.infllmv2_attn_varlen_func = infllmv2_attn_varlen_func
-    module.infllmv2_attn_stage1 = infllmv2_attn_stage1
-    module.max_pooling_1d_varlen = max_pooling_1d_varlen
+    if getattr(module, "infllmv2_attn_stage1", None) is None:
+        module.infllmv2_attn_stage1 = infllmv2_attn_stage1
+    if getattr(module, "max_pooling_1d_varlen", None) is None:
+        module.max_pooling_1d_varlen = max_pooling_1d_varlen
 
 
 def _sparse_forward(self, query_layer, key_layer, value_layer, cu_seqlens_q, cu_seqlens_k,

@@ -301,6 +301,36 @@ def test_sparse_attention_arbitrary_lists():
     assert ops.check_status(DEV) == 0
 
 
+def test_decode_step_through_sparse_forward_contract():
+    """Decode: one new query per sequence against its whole KV cache.
+
+    The reference decodes through the same ``sparse_forward`` call
+    (minicpm.py:3216-3244) with ``max_seqlen_q == 1``, i.e. ``causal=False``,
+    and page lists from its native decode selection.  Ragged cache lengths,
+    pages anywhere in the cache, -1 padding.
+    """
+    cache = [1500, 64, 777, 4096]
+    heads, groups = 32, 2
+    inp = ora.synthetic_layer(cache, num_heads=heads, num_kv_heads=groups, head_dim=128,
+                              router_heads=4, router_dim=32, hot_pages=2, seed=81, bf16=True)
+    last = inp.cu_seqlens[1:] - 1                     # the newest token of each sequence
+    q = inp.q[last]
+    cu_q = np.arange(len(cache) + 1, dtype=np.int32)
+    rng = np.random.default_rng(9)
+    idx = np.full((groups, len(cache), 12), -1, dtype=np.int32)
+    for b, n in enumerate(cache):
+        pages = (n + 63) // 64
+        for g in range(groups):
+            pick = rng.choice(pages, size=min(pages, 10), replace=False)
+            idx[g, b, :len(pick)] = pick
+    out = lsb.infllmv2_attn_varlen_func(
+        to_dev(q), to_dev(inp.k), to_dev(inp.v), cu_dev(cu_q), cu_dev(inp.cu_seqlens), 1,
+        max(cache), causal=False, topk_idx=to_dev(idx, torch.int32))
+    want, _ = ora.sparse_attention(q, inp.k, inp.v, cu_q, inp.cu_seqlens, idx, causal=False)
+    _attn_check(out, None, want, None)
+    assert ops.check_status(DEV) == 0
+
+
 def test_sparse_attention_flags_out_of_range_pages():
     lens = [200]
     inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,

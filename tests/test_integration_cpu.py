@@ -1,6 +1,8 @@
 """Wiring of the reference-model integration shim (CPU, no kernel launches)."""
 import types
 
+import pytest
+
 import torch
 from torch import nn
 
@@ -66,3 +68,19 @@ def test_module_symbols_satisfy_the_presence_check():
     integration.install_module_symbols(mod)
     for name in ("infllmv2_attn_stage1", "infllmv2_attn_varlen_func", "max_pooling_1d_varlen"):
         assert callable(getattr(mod, name))
+
+
+def test_module_symbols_keep_the_native_stage1_when_present():
+    """The reference's own stage-1 (native decode selection) survives install."""
+    def stage1(*args, **kwargs):
+        return "native"
+
+    mod = types.ModuleType("fake_minicpm")
+    mod.infllmv2_attn_stage1 = stage1
+    mod.max_pooling_1d_varlen = None
+    mod.infllmv2_attn_varlen_func = None
+    integration.install_module_symbols(mod)
+    assert mod.infllmv2_attn_stage1 is stage1
+    assert mod.infllmv2_attn_varlen_func is lsb.infllmv2_attn_varlen_func
+    with pytest.raises(NotImplementedError):
+        mod.max_pooling_1d_varlen()
