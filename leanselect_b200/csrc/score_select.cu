@@ -562,14 +562,30 @@ struct BufIndex {
   __device__ __forceinline__ int operator()(int j) const { return idx[j]; }
 };
 
-// Top-T' of each (group, query) row.  Rows with more than kDirectMax
-// candidates first estimate a cut from a 1/8 sample (every 8th group of 32
-// consecutive candidates, linear histogram between the sample's min and max,
-// aiming at ~1.5x the needed count), then keep the candidates at or above it
-// in a shared-memory buffer in one pass and select exactly among those.
-// The exact radix over the whole row runs for short rows and whenever the
-// estimate kept too few or too many candidates.  The result is identical
-// either way.
+// Exclusive prefix sum over the warp; returns it and sets `total`.
+__device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  total = __shfl_sync(0xffffffffu, incl, 31);
+  return incl - v;
+}
+
+constexpr int kUnroll = 4;  // float4 loads in flight per lane
+
+// Top-T' of each (group, query) row, one warp per row.  The row's candidate
+// scores are read with 16-byte loads, kUnroll per lane in flight.  Rows with
+// at most kBufCap candidates are copied once into a per-warp shared-memory
+// buffer (as order-preserving keys) and selected there.  Longer rows first
+// estimate a cut from a 1/8 sample (every 8th group of 128 consecutive
+// candidates; linear histogram between the sample's min and max, aiming at
+// ~1.5x the needed count), keep the candidates at or above it in the buffer
+// in one pass and select exactly among those; when the estimate kept too
+// few or too many, the exact radix runs over the whole row.  The result is
+// the same on every path: the T' largest scores, ties to the lower page.
 __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_constant__ ScoreArgs args) {
   __shared__ uint32_t hist_all[kTopkWarps][256];
   __shared__ uint32_t buf_key_all[kTopkWarps][kBufCap];
@@ -633,50 +649,101 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
     // the score kernel in slot n_init + m, the first non-sink local page.
     const int sinks_out = min(n_init, take_b);
     for (int k = lane; k < sinks_out; k += 32) out[k] = k;
-    const float* cand = scores + n_init;
-    const RowKeys row_keys{cand};
+    const RowKeys row_keys{scores + n_init};
     int k_out = sinks_out;
 
     if (cap > 0) {
+      // Candidates occupy row positions [n_init, end); rows are 32-byte aligned.
+      const float4* row4 = reinterpret_cast<const float4*>(scores);
+      const int end = n_init + m_all;
+      const int jb = n_init >> 2, je = (end + 3) >> 2;
       bool done = false;
-      if (m_all > kDirectMax) {
+      if (m_all <= kBufCap) {
+        // ---- copy the row's keys to shared memory, select there.
+        int finite = 0;
+        for (int base = jb; base < je; base += 32 * kUnroll) {
+          float4 v[kUnroll];
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            const int j = base + 32 * u + lane;
+            v[u] = j < je ? row4[j] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+          }
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            const int p0 = 4 * (base + 32 * u + lane);
+            const float vals[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = p0 + e - n_init;
+              if (i >= 0 && i < m_all) {
+                const uint32_t key = score_key(vals[e]);
+                buf_key[i] = key;
+                finite += key != 0u;
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) finite += __shfl_xor_sync(0xffffffffu, finite, o);
+        __syncwarp();
+        const BufKeys bk{buf_key};
+        const bool all = finite <= cap;
+        int need = cap;
+        const uint32_t thr = all ? 0u : radix_threshold(bk, m_all, need, hist, lane);
+        k_out = emit_selected(bk, Identity{}, m_all, all, thr, need, future, n_init, out, k_out, lane);
+        done = true;
+      } else {
         // ---- 1/8 sample: min, max and count of the finite sampled scores.
         float smin = INFINITY, smax = -INFINITY;
-        int fs = 0, sampled = 0;
-        for (int b0 = 0; b0 < m_all; b0 += 256) {
-          const int i = b0 + lane;
-          sampled += min(32, m_all - b0);
-          if (i < m_all) {
-            const float v = cand[i];
-            if (v > -INFINITY) {
-              ++fs;
-              smin = fminf(smin, v);
-              smax = fmaxf(smax, v);
+        int fs = 0, ns = 0;                              // finite / all sampled candidates
+        const int nblk = (je - jb + 31) >> 5;            // groups of 32 float4 (128 scores)
+        const int sampled_blocks = (nblk + 7) >> 3;
+        for (int sb = 0; sb < sampled_blocks; ++sb) {
+          const int j = jb + 256 * sb + lane;
+          if (j < je) {
+            const float4 v = row4[j];
+            const float vals[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 4 * j + e - n_init;
+              ns += (i >= 0 && i < m_all) ? 1 : 0;
+              if (i >= 0 && i < m_all && vals[e] > -INFINITY) {
+                ++fs;
+                smin = fminf(smin, vals[e]);
+                smax = fmaxf(smax, vals[e]);
+              }
             }
           }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
           fs += __shfl_xor_sync(0xffffffffu, fs, o);
+          ns += __shfl_xor_sync(0xffffffffu, ns, o);
           smin = fminf(smin, __shfl_xor_sync(0xffffffffu, smin, o));
           smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
         }
         uint32_t cut = 1u;  // keep every finite key unless the sample says better
         if (fs > 0 && smax > smin) {
           // Linear 128-bin histogram of the sample; the cut is the lower edge of
-          // the bin where the count from the top reaches ~1.5 cap * sampled/m_all.
+          // the bin where the count from the top reaches ~1.5 cap * fs / m_all.
           const float scale = 128.f / (smax - smin);
           for (int k = lane; k < 128; k += 32) hist[k] = 0;
           __syncwarp();
-          for (int b0 = 0; b0 < m_all; b0 += 256) {
-            const int i = b0 + lane;
-            if (i < m_all) {
-              const float v = cand[i];
-              if (v > -INFINITY) atomicAdd(&hist[min(127, static_cast<int>((v - smin) * scale))], 1u);
+          for (int sb = 0; sb < sampled_blocks; ++sb) {
+            const int j = jb + 256 * sb + lane;
+            if (j < je) {
+              const float4 v = row4[j];
+              const float vals[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int i = 4 * j + e - n_init;
+                if (i >= 0 && i < m_all && vals[e] > -INFINITY)
+                  atomicAdd(&hist[min(127, static_cast<int>((vals[e] - smin) * scale))], 1u);
+              }
             }
           }
           __syncwarp();
-          const int target = max(1, min(fs, static_cast<int>(1.5f * cap * sampled / m_all) + 1));
+          const int target = max(1, min(fs, static_cast<int>(1.5f * cap * ns / m_all) + 1));
           uint32_t c4[4];
           uint32_t lane_sum = 0;
 #pragma unroll
@@ -711,29 +778,49 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
           }
           __syncwarp();
         }
-        // ---- one pass: count finite candidates, keep those at or above the cut.
+        // ---- one pass: count finite candidates, keep those at or above the cut
+        // (in candidate order).
         int kept = 0, finite = 0;
         bool overflow = false;
-        for (int b0 = 0; b0 < m_all; b0 += 32) {
-          const int i = b0 + lane;
-          const uint32_t key = i < m_all ? row_keys(i) : 0u;
-          finite += __popc(__ballot_sync(0xffffffffu, key != 0u));
-          const bool keep = key >= cut && key != 0u;
-          const uint32_t keep_mask = __ballot_sync(0xffffffffu, keep);
-          const int nk = __popc(keep_mask);
-          if (!overflow) {
-            if (kept + nk > kBufCap) {
-              overflow = true;
-            } else {
-              if (keep) {
-                const int at = kept + __popc(keep_mask & ((1u << lane) - 1));
-                buf_key[at] = key;
-                buf_idx[at] = i;
+        for (int base = jb; base < je; base += 32 * kUnroll) {
+          float4 v[kUnroll];
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            const int j = base + 32 * u + lane;
+            v[u] = j < je ? row4[j] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+          }
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            const int p0 = 4 * (base + 32 * u + lane);
+            const float vals[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+            uint32_t keys[4];
+            int mine = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = p0 + e - n_init;
+              keys[e] = (i >= 0 && i < m_all) ? score_key(vals[e]) : 0u;
+              finite += keys[e] != 0u;
+              mine += (keys[e] >= cut && keys[e] != 0u) ? 1 : 0;
+            }
+            int total;
+            const int at = kept + warp_excl_scan(mine, lane, total);
+            if (!overflow && kept + total > kBufCap) overflow = true;
+            if (!overflow) {
+              int w = at;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                if (keys[e] >= cut && keys[e] != 0u) {
+                  buf_key[w] = keys[e];
+                  buf_idx[w] = p0 + e - n_init;
+                  ++w;
+                }
               }
-              kept += nk;
+              kept += total;
             }
           }
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) finite += __shfl_xor_sync(0xffffffffu, finite, o);
         __syncwarp();
         if (finite <= cap) {
           k_out = emit_selected(row_keys, Identity{}, m_all, true, 0u, 0, future, n_init, out, k_out,
@@ -761,6 +848,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
         k_out = emit_selected(row_keys, Identity{}, m_all, all, thr, need, future, n_init, out, k_out,
                               lane);
       }
+      __syncwarp();
     }
     // Local pages (those that are not sinks), then padding.
     const int local_out = max(0, min(n_local, take_b - k_out));

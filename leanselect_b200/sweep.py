@@ -56,8 +56,10 @@ def config1_layer(n: int, device: torch.device, seed: int = 0, num_heads: int = 
 
 def make_selector(device: torch.device, seed: int = 0, num_heads: int = 32,
                   num_kv_heads: int = 2) -> LeanSelectSelector:
-    sel = LeanSelectSelector(num_heads=num_heads, num_kv_heads=num_kv_heads, head_dim=128,
-                             router_heads=32, router_dim=4)
+    with torch.random.fork_rng(devices=[]):
+        torch.manual_seed(seed)  # the projections' own initialisation, identical on every rank
+        sel = LeanSelectSelector(num_heads=num_heads, num_kv_heads=num_kv_heads, head_dim=128,
+                                 router_heads=32, router_dim=4)
     gen = torch.Generator().manual_seed(seed + 1)
     with torch.no_grad():
         sel.head_mix.copy_(torch.randn(sel.head_mix.shape, generator=gen) / math.sqrt(32))
