@@ -142,7 +142,7 @@ int ls_score_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
                    int32_t kernel_stride, float* page_scores, int32_t* status, void* stream);
 
 /*
- * ls_atom_scores -- replaces NOSA's LlamaAttention._leanselect_atom_scores
+ * ls_atom_scores -- replaces NOSA's LlamaSdpaAttention._leanselect_atom_scores
  * (leanselect/models/nosa.py:1822-1853): raw LeanSelect atom scores
  * Qs[t]·Ks[a] for every (group, query row, atom of its sequence), no causal
  * mask, as bf16 [G, total_q, max_atoms] (max_atoms = the batch's largest atom

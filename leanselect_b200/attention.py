@@ -95,7 +95,7 @@ def lightweight_compressed_attention(module, q_unpad: torch.Tensor, k_compressed
 def nosa_atom_scores(module, query_layer: torch.Tensor, compressed_k: torch.Tensor,
                      cu_seqlens_q: torch.Tensor, compressed_cu_seqlens: torch.Tensor,
                      q_lengths=None, c_lengths=None) -> torch.Tensor:
-    """NOSA's ``LlamaAttention._leanselect_atom_scores`` (nosa.py:1822-1853).
+    """NOSA's ``LlamaSdpaAttention._leanselect_atom_scores`` (nosa.py:1822-1853).
 
     ``[G, total_q, max_atoms]`` raw LeanSelect atom scores in the query dtype,
     ``-inf`` past each sequence's atoms, for NOSA's ``compressed_attention``

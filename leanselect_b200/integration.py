@@ -9,7 +9,7 @@ For a model loaded with the reference's ``load_model(..., method="leanselect")``
     install(model)
 
 ``install`` patches every ``MiniCPMInfLLMv2Attention`` (minicpm.py:1948) and
-every module that owns a ``leanselect`` selector (NOSA's ``LlamaAttention``,
+every module that owns a ``leanselect`` selector (NOSA's ``LlamaSdpaAttention``,
 nosa.py:1822-1853):
 
 * ``compress_k`` / ``compress_k2`` -> :class:`leanselect_b200.CompressK`

@@ -254,6 +254,31 @@ def uniform_cases():
     np.savez_compressed(HERE / "uniform_selection.npz", **flat)
 
 
+def nosa_atom_score_cases():
+    """NOSA's ``LlamaSdpaAttention._leanselect_atom_scores`` (nosa.py:1822-1853), bf16.
+
+    Called unbound on a namespace carrying the selector and the KV-head count,
+    on a ragged pack that includes a sequence too short for any atom.
+    """
+    from leanselect.models.nosa import LlamaSdpaAttention
+
+    lens = [700, 20, 1333]
+    inputs = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128,
+                                 router_heads=4, router_dim=32, hot_pages=3, seed=97, bf16=True)
+    kc, cu_c = CompressK(2, 128, kernel_size=32, kernel_stride=16)(
+        torch.from_numpy(inputs.k).bfloat16(), torch.from_numpy(inputs.cu_seqlens))
+    sel = make_selector(inputs.params)  # fp32 parameters, bf16 activations (fused_weights casts)
+    ns = SimpleNamespace(leanselect=sel, num_key_value_heads=2)
+    with torch.no_grad():
+        scores = LlamaSdpaAttention._leanselect_atom_scores(
+            ns, torch.from_numpy(inputs.q).bfloat16(), kc, torch.from_numpy(inputs.cu_seqlens),
+            cu_c)
+    np.savez_compressed(
+        HERE / "nosa_atom_scores.npz", seed=np.int64(97), lens=np.array(lens, dtype=np.int64),
+        input_digest=np.array(digest(inputs.q, inputs.k, inputs.v)), cu_c=cu_c.numpy(),
+        scores_bits=scores.view(torch.int16).numpy())
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
     known_answers()
@@ -263,5 +288,6 @@ if __name__ == "__main__":
     config0_case()
     bf16_selection_case()
     uniform_cases()
+    nosa_atom_score_cases()
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)

@@ -531,3 +531,22 @@ def test_uniform_config1_rows():
     want = ora.Selection(idx, bnd, [(0, masked)])
     bad = ora.uniform_selection_mismatches(got[:, rows], want, rel_tol=2 ** -7, positions=rows)
     assert not bad, bad[:5]
+
+
+def test_nosa_atom_scores_match_reference_fixture():
+    """GPU atom scores against the reference's own NOSA output (tests/golden)."""
+    import pathlib
+    g = np.load(pathlib.Path(__file__).parent / "golden" / "nosa_atom_scores.npz")
+    lens = g["lens"].tolist()
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=3, seed=int(g["seed"]), bf16=True)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    module = type("NosaLayer", (), {"leanselect": selector_for(inp.params)})()
+    got = lsb.nosa_atom_scores(module, to_dev(inp.q), to_dev(kc), cu_dev(inp.cu_seqlens),
+                               cu_dev(cu_c)).float().cpu().numpy()
+    ref = ora.from_bf16_bits(g["scores_bits"].view(np.uint16))
+    assert got.shape == ref.shape
+    finite = np.isfinite(ref)
+    assert np.array_equal(finite, np.isfinite(got))
+    np.testing.assert_allclose(got[finite], ref[finite], rtol=2 ** -7, atol=2e-3)
+    assert np.mean(got[finite] == ref[finite]) > 0.95

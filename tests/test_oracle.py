@@ -314,3 +314,28 @@ def test_uniform_future_page_takes_a_slot():
     sel, _, _ = ora.uniform_select_rows(atoms, [360], seq_len=n, take=3, topk=3,
                                         init_blocks=1, local_blocks=0)
     assert sorted(sel[0, 0].tolist()) == [0, 1, 5]    # atom 23 not visible yet at token 360
+
+
+def test_nosa_atom_scores_match_reference():
+    """Raw atom scores of NOSA's precomputed-score path (nosa.py:1822-1853), bf16."""
+    g = load("nosa_atom_scores.npz")
+    lens = g["lens"].tolist()
+    inputs = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                                 router_dim=32, hot_pages=3, seed=int(g["seed"]), bf16=True)
+    assert digest(inputs.q, inputs.k, inputs.v) == str(g["input_digest"])
+    kc, cu_c = ora.compress_keys(inputs.k, inputs.cu_seqlens, policy="bf16")
+    np.testing.assert_array_equal(cu_c, g["cu_c"])
+    ref = ora.from_bf16_bits(g["scores_bits"].view(np.uint16))
+    qf, kf = ora.fold_weights(inputs.params, "bf16")
+    for b, n in enumerate(lens):
+        q0, c0, c1 = inputs.cu_seqlens[b], cu_c[b], cu_c[b + 1]
+        rows = ref[:, q0:q0 + n]
+        if c1 > c0:
+            want = ora.bf16_round(ora.atom_scores(
+                ora.project_queries(inputs.q[q0:q0 + n], qf, 2, "bf16"),
+                ora.project_atom_keys(kc[c0:c1], kf, "bf16")))
+            got = rows[..., :c1 - c0]
+            # Same bf16 inputs; only the fp32 accumulation order differs.
+            np.testing.assert_allclose(got, want, rtol=2 ** -7, atol=2e-3)
+            assert np.mean(got == want) > 0.95
+        assert np.all(np.isneginf(rows[..., c1 - c0:]))
