@@ -7,16 +7,15 @@ from __future__ import annotations
 
 import torch
 
-from . import _native
-from .ops import _require_cuda, _stream
+from .ops import _call, _require_cuda, _stream
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     dev = _require_cuda(x, weight)
     x = x.contiguous()
     out = torch.empty_like(x)
-    _native.call("ls_bb_rms_norm", x.data_ptr(), weight.data_ptr(), x.numel() // x.shape[-1],
-                 x.shape[-1], float(eps), out.data_ptr(), _stream(dev))
+    _call(dev, "ls_bb_rms_norm", x.data_ptr(), weight.data_ptr(), x.numel() // x.shape[-1],
+               x.shape[-1], float(eps), out.data_ptr(), _stream(dev))
     return out
 
 
@@ -31,9 +30,9 @@ def rope_split(qkv: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tenso
     q = torch.empty(n, num_heads, head_dim, dtype=qkv.dtype, device=dev)
     k = torch.empty(n, num_kv_heads, head_dim, dtype=qkv.dtype, device=dev)
     v = torch.empty(n, num_kv_heads, head_dim, dtype=qkv.dtype, device=dev)
-    _native.call("ls_bb_rope_split", qkv.data_ptr(), pos.data_ptr(), inv.data_ptr(),
-                 float(scaling), n, num_heads, num_kv_heads, head_dim, q.data_ptr(), k.data_ptr(),
-                 v.data_ptr(), _stream(dev))
+    _call(dev, "ls_bb_rope_split", qkv.data_ptr(), pos.data_ptr(), inv.data_ptr(),
+               float(scaling), n, num_heads, num_kv_heads, head_dim, q.data_ptr(), k.data_ptr(),
+               v.data_ptr(), _stream(dev))
     return q, k, v
 
 
@@ -42,5 +41,5 @@ def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
     gate_up = gate_up.contiguous()
     n, two_i = gate_up.shape
     out = torch.empty(n, two_i // 2, dtype=gate_up.dtype, device=dev)
-    _native.call("ls_bb_silu_mul", gate_up.data_ptr(), n, two_i // 2, out.data_ptr(), _stream(dev))
+    _call(dev, "ls_bb_silu_mul", gate_up.data_ptr(), n, two_i // 2, out.data_ptr(), _stream(dev))
     return out

@@ -38,6 +38,13 @@ def _require_cuda(*tensors: torch.Tensor) -> torch.device:
     return dev
 
 
+def _call(dev: torch.device, name: str, *args) -> None:
+    """One C-ABI call with ``dev`` as the current device (the kernels launch on
+    the calling thread's current device; the reference guards the same way)."""
+    with torch.cuda.device(dev):
+        _native.call(name, *args)
+
+
 def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
@@ -135,30 +142,30 @@ def fold_weights(head_mix: torch.Tensor, kv_head_mix: torch.Tensor, q_proj: torc
         if dtype in (None, torch.float32):
             qf = torch.empty(H, D, F, dtype=torch.float32, device=dev)
             kf = torch.empty(G, D, F, dtype=torch.float32, device=dev)
-            _native.call("ls_fold_weights", hm.data_ptr(), km.data_ptr(), qp.data_ptr(),
-                         kp.data_ptr(), H, G, D, R, r, qf.data_ptr(), kf.data_ptr(), None, None,
-                         None, None, s)
+            _call(dev, "ls_fold_weights", hm.data_ptr(), km.data_ptr(), qp.data_ptr(),
+                       kp.data_ptr(), H, G, D, R, r, qf.data_ptr(), kf.data_ptr(), None, None,
+                       None, None, s)
             if dtype is None or dtype == torch.float32:
                 return qf, kf
         if dtype == torch.bfloat16:
             qb = torch.empty(H, D, F, dtype=torch.bfloat16, device=dev)
             kb = torch.empty(G, D, F, dtype=torch.bfloat16, device=dev)
-            _native.call("ls_fold_weights", hm.data_ptr(), km.data_ptr(), qp.data_ptr(),
-                         kp.data_ptr(), H, G, D, R, r, None, None, qb.data_ptr(), kb.data_ptr(),
-                         None, None, s)
+            _call(dev, "ls_fold_weights", hm.data_ptr(), km.data_ptr(), qp.data_ptr(),
+                       kp.data_ptr(), H, G, D, R, r, None, None, qb.data_ptr(), kb.data_ptr(),
+                       None, None, s)
             return qb, kb
         # Other dtypes: the reference casts the fp32 product (selector.py:155-157).
         qf = torch.empty(H, D, F, dtype=torch.float32, device=dev)
         kf = torch.empty(G, D, F, dtype=torch.float32, device=dev)
-        _native.call("ls_fold_weights", hm.data_ptr(), km.data_ptr(), qp.data_ptr(),
-                     kp.data_ptr(), H, G, D, R, r, qf.data_ptr(), kf.data_ptr(), None, None,
-                     None, None, s)
+        _call(dev, "ls_fold_weights", hm.data_ptr(), km.data_ptr(), qp.data_ptr(),
+                   kp.data_ptr(), H, G, D, R, r, qf.data_ptr(), kf.data_ptr(), None, None,
+                   None, None, s)
         return qf.to(dtype), kf.to(dtype)
     hg = H // G
     wq_t = torch.empty(G, F, hg * D, dtype=torch.bfloat16, device=dev)
     wk_t = torch.empty(G, F, D, dtype=torch.bfloat16, device=dev)
-    _native.call("ls_fold_weights", hm.data_ptr(), km.data_ptr(), qp.data_ptr(), kp.data_ptr(),
-                 H, G, D, R, r, None, None, None, None, wq_t.data_ptr(), wk_t.data_ptr(), s)
+    _call(dev, "ls_fold_weights", hm.data_ptr(), km.data_ptr(), qp.data_ptr(), kp.data_ptr(),
+               H, G, D, R, r, None, None, None, None, wq_t.data_ptr(), wk_t.data_ptr(), s)
     return FoldedWeights(wq_t, wk_t, H, G, D, F)
 
 
@@ -172,30 +179,33 @@ def compressed_seqlens(cu_seqlens_k: torch.Tensor, kernel_size: int = 32,
     dev = _require_cuda(cu_seqlens_k)
     cu = _i32(cu_seqlens_k)
     out = torch.empty_like(cu)
-    _native.call("ls_compressed_seqlens", cu.data_ptr(), cu.numel() - 1, kernel_size,
-                 kernel_stride, out.data_ptr(), status_word(dev).data_ptr(), _stream(dev))
+    _call(dev, "ls_compressed_seqlens", cu.data_ptr(), cu.numel() - 1, kernel_size,
+               kernel_stride, out.data_ptr(), status_word(dev).data_ptr(), _stream(dev))
     return out
 
 
 def compress_keys(k: torch.Tensor, cu_seqlens_k: torch.Tensor, *, kernel_size: int = 32,
-                  kernel_stride: int = 16, lengths: Sequence[int] | None = None):
+                  kernel_stride: int = 16, lengths: Sequence[int] | None = None,
+                  total_c: int | None = None):
     """``CompressK.forward`` (minicpm.py:1169-1185): ``k [total_k, G, D] -> (kc, cu_c)``.
 
-    ``lengths`` (host sequence lengths) avoids the device->host copy of
-    ``cu_seqlens_k`` that sizing the output otherwise needs.
+    ``lengths`` (host sequence lengths) or ``total_c`` (the number of atoms)
+    avoids the device->host copy of ``cu_seqlens_k`` that sizing the output
+    otherwise needs.
     """
     dev = _require_cuda(k, cu_seqlens_k)
     if k.ndim != 3:
         raise ValueError("k must be [total_k, num_kv_heads, head_dim]")
     kb = _bf16(k)
     cu = _i32(cu_seqlens_k)
-    lens = list(lengths) if lengths is not None else host_lengths(cu)
-    total_c = sum(atom_count(n, kernel_size, kernel_stride) for n in lens)
+    if total_c is None:
+        lens = list(lengths) if lengths is not None else host_lengths(cu)
+        total_c = sum(atom_count(n, kernel_size, kernel_stride) for n in lens)
     kc = torch.empty(total_c, k.shape[1], k.shape[2], dtype=torch.bfloat16, device=dev)
     cu_c = torch.empty_like(cu)
-    _native.call("ls_compress_keys", kb.data_ptr(), cu.data_ptr(), cu.numel() - 1, kb.shape[0],
-                 k.shape[1], k.shape[2], kernel_size, kernel_stride, _ptr(kc) if total_c else None,
-                 cu_c.data_ptr(), total_c, status_word(dev).data_ptr(), _stream(dev))
+    _call(dev, "ls_compress_keys", kb.data_ptr(), cu.data_ptr(), cu.numel() - 1, kb.shape[0],
+               k.shape[1], k.shape[2], kernel_size, kernel_stride, _ptr(kc) if total_c else None,
+               cu_c.data_ptr(), total_c, status_word(dev).data_ptr(), _stream(dev))
     return kc, cu_c
 
 
@@ -211,8 +221,8 @@ def project_atom_keys(kc: torch.Tensor, wk_t: torch.Tensor) -> torch.Tensor:
     F = wk_t.shape[1]
     ks = torch.empty(G, A, F, dtype=torch.bfloat16, device=dev)
     if A:
-        _native.call("ls_project_atom_keys", kcb.data_ptr(), A, G, D, wk_t.data_ptr(), F,
-                     ks.data_ptr(), _stream(dev))
+        _call(dev, "ls_project_atom_keys", kcb.data_ptr(), A, G, D, wk_t.data_ptr(), F,
+                   ks.data_ptr(), _stream(dev))
     return ks
 
 
@@ -224,8 +234,8 @@ def project_queries(q: torch.Tensor, wq_t: torch.Tensor, num_kv_heads: int) -> t
     F = wq_t.shape[1]
     qs = torch.empty(num_kv_heads, N, F, dtype=torch.bfloat16, device=dev)
     if N:
-        _native.call("ls_project_queries", qb.data_ptr(), N, H, num_kv_heads, D, wq_t.data_ptr(),
-                     F, qs.data_ptr(), status_word(dev).data_ptr(), _stream(dev))
+        _call(dev, "ls_project_queries", qb.data_ptr(), N, H, num_kv_heads, D, wq_t.data_ptr(),
+                   F, qs.data_ptr(), status_word(dev).data_ptr(), _stream(dev))
     return qs
 
 
@@ -245,11 +255,11 @@ def score_pages(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
     pages = (int(max_seqlen_q) + block_size - 1) // block_size
     out = torch.empty(G, total_q, pages, dtype=torch.float32, device=dev)
     cu_q, cu_c = _i32(cu_seqlens_q), _i32(cu_seqlens_c)
-    _native.call("ls_score_pages", qb.data_ptr(), weights.wq_t.data_ptr(),
-                 _ptr(ks) if total_c else None, cu_q.data_ptr(), cu_c.data_ptr(),
-                 cu_q.numel() - 1, int(max_seqlen_q), total_q, total_c, weights.num_heads, G,
-                 weights.head_dim, weights.width, block_size, kernel_stride, out.data_ptr(),
-                 status_word(dev).data_ptr(), _stream(dev))
+    _call(dev, "ls_score_pages", qb.data_ptr(), weights.wq_t.data_ptr(),
+               _ptr(ks) if total_c else None, cu_q.data_ptr(), cu_c.data_ptr(),
+               cu_q.numel() - 1, int(max_seqlen_q), total_q, total_c, weights.num_heads, G,
+               weights.head_dim, weights.width, block_size, kernel_stride, out.data_ptr(),
+               status_word(dev).data_ptr(), _stream(dev))
     return out
 
 
@@ -266,11 +276,11 @@ def atom_scores(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
     if total_q == 0 or max_atoms == 0:
         return out
     cu_q, cu_c = _i32(cu_seqlens_q), _i32(cu_seqlens_c)
-    _native.call("ls_atom_scores", qb.data_ptr(), weights.wq_t.data_ptr(),
-                 _ptr(ks) if total_c else None, cu_q.data_ptr(), cu_c.data_ptr(),
-                 cu_q.numel() - 1, int(max_seqlen_q), total_q, total_c, weights.num_heads, G,
-                 weights.head_dim, weights.width, int(max_atoms), out.data_ptr(),
-                 status_word(dev).data_ptr(), _stream(dev))
+    _call(dev, "ls_atom_scores", qb.data_ptr(), weights.wq_t.data_ptr(),
+               _ptr(ks) if total_c else None, cu_q.data_ptr(), cu_c.data_ptr(),
+               cu_q.numel() - 1, int(max_seqlen_q), total_q, total_c, weights.num_heads, G,
+               weights.head_dim, weights.width, int(max_atoms), out.data_ptr(),
+               status_word(dev).data_ptr(), _stream(dev))
     return out
 
 
@@ -291,12 +301,12 @@ def select_pages(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
         return idx
     cu_q, cu_c = _i32(cu_seqlens_q), _i32(cu_seqlens_c)
     ws = _workspace(dev, total_q, G, int(max_seqlen_q))
-    _native.call("ls_select_pages", qb.data_ptr(), weights.wq_t.data_ptr(),
-                 _ptr(ks) if total_c else None, cu_q.data_ptr(), cu_c.data_ptr(),
-                 cu_q.numel() - 1, int(max_seqlen_q), total_q, total_c, weights.num_heads, G,
-                 weights.head_dim, weights.width, int(take), int(init_blocks), int(local_blocks),
-                 block_size, kernel_stride, idx.data_ptr(), ws.data_ptr(), ws.numel(),
-                 status_word(dev).data_ptr(), _stream(dev))
+    _call(dev, "ls_select_pages", qb.data_ptr(), weights.wq_t.data_ptr(),
+               _ptr(ks) if total_c else None, cu_q.data_ptr(), cu_c.data_ptr(),
+               cu_q.numel() - 1, int(max_seqlen_q), total_q, total_c, weights.num_heads, G,
+               weights.head_dim, weights.width, int(take), int(init_blocks), int(local_blocks),
+               block_size, kernel_stride, idx.data_ptr(), ws.data_ptr(), ws.numel(),
+               status_word(dev).data_ptr(), _stream(dev))
     return idx
 
 
@@ -322,11 +332,11 @@ def uniform_select_pages(q: torch.Tensor, kc: torch.Tensor, cu_seqlens_q: torch.
     nbytes = _native.load().ls_uniform_select_workspace_bytes(total_q, total_c, H, G,
                                                               int(max_seqlen_q))
     ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=dev)
-    _native.call("ls_uniform_select_pages", qb.data_ptr(), kcb.data_ptr() if total_c else None,
-                 cu_q.data_ptr(), cu_c.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q), total_q,
-                 total_c, H, G, D, int(take), int(init_blocks), int(local_blocks), block_size,
-                 kernel_stride, float(softmax_scale or 0.0), idx.data_ptr(), ws.data_ptr(),
-                 ws.numel(), status_word(dev).data_ptr(), _stream(dev))
+    _call(dev, "ls_uniform_select_pages", qb.data_ptr(), kcb.data_ptr() if total_c else None,
+               cu_q.data_ptr(), cu_c.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q), total_q,
+               total_c, H, G, D, int(take), int(init_blocks), int(local_blocks), block_size,
+               kernel_stride, float(softmax_scale or 0.0), idx.data_ptr(), ws.data_ptr(),
+               ws.numel(), status_word(dev).data_ptr(), _stream(dev))
     return idx
 
 
@@ -356,11 +366,11 @@ def select_pages_chunk(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor
     if take == 0 or n == 0:
         return idx
     ws = _workspace(dev, n, G, int(seq_len))
-    _native.call("ls_select_pages_chunk", qb.data_ptr(), weights.wq_t.data_ptr(),
-                 _ptr(ks) if total_c else None, n, int(q_position), int(seq_len), total_c,
-                 weights.num_heads, G, weights.head_dim, weights.width, int(take),
-                 int(init_blocks), int(local_blocks), block_size, kernel_stride, idx.data_ptr(),
-                 ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(), _stream(dev))
+    _call(dev, "ls_select_pages_chunk", qb.data_ptr(), weights.wq_t.data_ptr(),
+               _ptr(ks) if total_c else None, n, int(q_position), int(seq_len), total_c,
+               weights.num_heads, G, weights.head_dim, weights.width, int(take),
+               int(init_blocks), int(local_blocks), block_size, kernel_stride, idx.data_ptr(),
+               ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(), _stream(dev))
     return idx
 
 
@@ -386,11 +396,11 @@ def sparse_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q:
     lse = torch.empty(H, total_q, dtype=torch.float32, device=dev) if return_lse else None
     cu_q, cu_k = _i32(cu_seqlens_q), _i32(cu_seqlens_k)
     scale = float(softmax_scale) if softmax_scale is not None else 1.0 / math.sqrt(D)
-    _native.call("ls_sparse_attn", qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), cu_q.data_ptr(),
-                 cu_k.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q), int(max_seqlen_k),
-                 total_q, total_k, H, G, D, idx.data_ptr(), idx.shape[2], block_size, scale,
-                 1 if causal else 0, out.data_ptr(), _ptr(lse), status_word(dev).data_ptr(),
-                 _stream(dev))
+    _call(dev, "ls_sparse_attn", qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), cu_q.data_ptr(),
+               cu_k.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q), int(max_seqlen_k),
+               total_q, total_k, H, G, D, idx.data_ptr(), idx.shape[2], block_size, scale,
+               1 if causal else 0, out.data_ptr(), _ptr(lse), status_word(dev).data_ptr(),
+               _stream(dev))
     if q.dtype != torch.bfloat16:
         out = out.to(q.dtype)
     return (out, lse) if return_lse else out
@@ -413,7 +423,7 @@ def sparse_attn_gather_only(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if idx.ndim != 3 or idx.shape[0] != G or idx.shape[1] != total_q:
         raise ValueError("topk_idx must be [num_kv_heads, total_q, T]")
     cu_q, cu_k = _i32(cu_seqlens_q), _i32(cu_seqlens_k)
-    _native.call("ls_sparse_attn_gather_only", qb.data_ptr(), kb.data_ptr(), vb.data_ptr(),
-                 cu_q.data_ptr(), cu_k.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q),
-                 int(max_seqlen_k), total_q, total_k, H, G, D, idx.data_ptr(), idx.shape[2],
-                 block_size, 1 if causal else 0, status_word(dev).data_ptr(), _stream(dev))
+    _call(dev, "ls_sparse_attn_gather_only", qb.data_ptr(), kb.data_ptr(), vb.data_ptr(),
+               cu_q.data_ptr(), cu_k.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q),
+               int(max_seqlen_k), total_q, total_k, H, G, D, idx.data_ptr(), idx.shape[2],
+               block_size, 1 if causal else 0, status_word(dev).data_ptr(), _stream(dev))

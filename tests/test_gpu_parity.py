@@ -550,3 +550,28 @@ def test_nosa_atom_scores_match_reference_fixture():
     assert np.array_equal(finite, np.isfinite(got))
     np.testing.assert_allclose(got[finite], ref[finite], rtol=2 ** -7, atol=2e-3)
     assert np.mean(got[finite] == ref[finite]) > 0.95
+
+
+def test_torch_custom_ops_match_fake_shapes():
+    """torch.ops.leanselect_b200.* run the kernels; their fake shapes agree (opcheck)."""
+    import leanselect_b200.torch_ops  # noqa: F401
+    lens = [700, 333]
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=2, seed=12, bf16=True)
+    q, k, v = to_dev(inp.q), to_dev(inp.k), to_dev(inp.v)
+    cu = cu_dev(inp.cu_seqlens)
+    sel = selector_for(inp.params)
+    w = sel.kernel_weights()
+    total_c = sum(ops.atom_count(n) for n in lens)
+    kc, cu_c = torch.ops.leanselect_b200.compress_keys(k, cu, total_c, 32, 16)
+    ks = torch.ops.leanselect_b200.project_atom_keys(kc, w.wk_t)
+    idx = torch.ops.leanselect_b200.select_pages(q, w.wq_t, ks, cu, cu_c, max(lens), 9, 1, 2)
+    direct = ops.select_pages(q, w, ks, cu, cu_c, max(lens), take=9)
+    assert torch.equal(idx, direct)
+    checks = ("test_schema", "test_faketensor")
+    torch.library.opcheck(torch.ops.leanselect_b200.sparse_attn.default,
+                          (q, k, v, cu, cu, max(lens), max(lens), idx, 0.0, True),
+                          test_utils=checks)
+    torch.library.opcheck(torch.ops.leanselect_b200.select_pages.default,
+                          (q, w.wq_t, ks, cu, cu_c, max(lens), 9, 1, 2), test_utils=checks)
+    assert ops.check_status(DEV) == 0
