@@ -317,17 +317,22 @@ def run_ours(args):
     pk, pk_kind = peaks()
     layers = len(key_counts)
     hg = shape.num_heads // shape.num_kv_heads
-    flops_per_launch = 4 * shape.head_dim * hg * (sum(key_counts) / max(layers, 1))
-    attn_ms = statistics.mean(stage["attn"]) if stage["attn"] else float("nan")
-    achieved = flops_per_launch / (attn_ms / 1e3) / 1e12
+    # Per layer of this rank: one attention launch on a single GPU, two (the
+    # early and the late zig-zag chunk) when sequence-parallel; stage spans
+    # are summed per layer.
+    layer_steps = max(1, args.steps * layers)
+    stage_ms = {k: sum(v) / layer_steps for k, v in stage.items() if v}
+    flops_per_layer = 4 * shape.head_dim * hg * (sum(key_counts) / max(layers, 1))
+    attn_ms = stage_ms.get("attn", float("nan"))
+    achieved = flops_per_layer / (attn_ms / 1e3) / 1e12
     peak = pk["bf16_tflops_sustained"]
-    # Our kernels per layer: compressed seqlens, compression, key projection,
-    # then scoring, top-k and sparse attention once per query chunk (one chunk
-    # on a single GPU, two zig-zag chunks per rank when sequence-parallel);
-    # plus the host model's fused RMSNorm (2 + MLP chunks), RoPE and SiLU kernels.
+    # Our kernels per layer: per query chunk (one on a single GPU, two zig-zag
+    # chunks per rank when sequence-parallel) compressed seqlens, compression,
+    # key projection, scoring, top-k and sparse attention; plus the host
+    # model's fused RMSNorm (2 + MLP chunks), RoPE and SiLU kernels.
     chunks = 1 if world == 1 else 2
     mlp_chunks = -(-(n // world) // 16384)
-    launches_per_layer = 3 + 3 * chunks + (1 + 2 * mlp_chunks + 1)
+    launches_per_layer = 6 * chunks + (1 + 2 * mlp_chunks + 1)
     line = {
         "metric": METRIC,
         "value": value,
@@ -349,9 +354,8 @@ def run_ours(args):
             "parallelism": f"sp{world}" if world > 1 else "single",
             "l2": "working set larger than L2 (16 GB of weights, >=1 GB activations per layer)",
         },
-        "select_attn_ms_per_layer": (statistics.mean(stage["select"]) + attn_ms
-                                     + statistics.mean(stage["compress"])),
-        "stage_ms_per_layer": {k: statistics.mean(v) for k, v in stage.items() if v},
+        "select_attn_ms_per_layer": stage_ms["select"] + attn_ms + stage_ms["compress"],
+        "stage_ms_per_layer": stage_ms,
         "e2e": {"value": n / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": n * 8,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_layer * layers * args.steps,
@@ -363,7 +367,8 @@ def run_ours(args):
             "unit": "TFLOP/s",
             "frac": achieved / peak,
             "peak_kind": f"{pk_kind} (bf16 dense, sustained)",
-            "flops_per_launch": flops_per_launch,
+            "flops_per_layer": flops_per_layer,
+            "attn_launches_per_layer": chunks,
             # dram__bytes_read.sum + dram__bytes_write.sum per attention launch of
             # this command at 131072 tokens: mean of 24 launches captured in one
             # ncu pass (`--metrics gpu__time_duration.sum,dram__bytes_read.sum,

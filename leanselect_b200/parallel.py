@@ -81,26 +81,47 @@ def lpt_shards(lengths: Sequence[int], world: int) -> list[list[int]]:
 _CU_CACHE: dict[tuple, torch.Tensor] = {}
 
 
+_COMM_STREAMS: dict[int, torch.cuda.Stream] = {}
+
+
+def _comm_stream(dev: torch.device) -> torch.cuda.Stream:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    stream = _COMM_STREAMS.get(idx)
+    if stream is None:
+        stream = _COMM_STREAMS[idx] = torch.cuda.Stream(device=dev)
+    return stream
+
+
 def sequence_parallel_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_len: int,
                             selector, cfg, group=None, timers: list | None = None,
                             key_counts: list | None = None) -> torch.Tensor:
     """The hot path of one layer for this rank's two zig-zag query chunks.
 
     ``q [2C, H, D]``, ``k``/``v [2C, G, D]`` are this rank's rows (chunk ``r``
-    then chunk ``2W-1-r``, post-RoPE).  All-gathers K/V into the whole
-    sequence, compresses it, projects the atom keys, selects pages for the
-    local query rows at their true positions and runs the sparse attention
-    over each chunk's causal key prefix.  Returns the local attention output
-    ``[2C, H, D]``.  ``timers`` receives ``(stage, start, end)`` CUDA events
-    for "gather", "compress", "select" and "attn".
+    then chunk ``2W-1-r``, post-RoPE).  Returns the local attention output
+    ``[2C, H, D]``.
+
+    The early chunks of all ranks are sequence chunks ``0 .. W-1`` in rank
+    order, so they are all-gathered straight into the front half of the full
+    K/V.  That half is all the early chunk ``r`` needs (its keys end at
+    ``(r+1)C <= WC``, and so do the atoms its candidate pages pool), so its
+    compression, selection and attention run while the late chunks are
+    all-gathered on a second stream; the late half is then put in sequence
+    order, the whole K compressed, and the late chunk selected and attended.
+    The result equals gathering everything first.  ``timers`` receives
+    ``(stage, start, end)`` CUDA events for "gather", "compress", "select" and
+    "attn" (two spans per stage: early chunk, late chunk).
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     n = int(seq_len)
     chunks = zigzag_chunks(n, world, rank)
     c = chunks[0][1]
+    half = world * c
     g, d = k.shape[1], k.shape[2]
     dev = q.device
+    compute = torch.cuda.current_stream(dev)
+    comm = _comm_stream(dev)
 
     def mark():
         if timers is None:
@@ -116,40 +137,65 @@ def sequence_parallel_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s
             t = _CU_CACHE[key] = torch.tensor(values, dtype=torch.int32, device=dev)
         return t
 
-    e_g = mark()
-    kv = torch.stack((k.reshape(2 * c, -1), v.reshape(2 * c, -1)), dim=1)
-    full = gather_sequence(kv, n, group)                 # [n, 2, G*D]
-    k_full = full[:, 0].reshape(n, g, d).contiguous()
-    v_full = full[:, 1].reshape(n, g, d).contiguous()
-    del kv, full
-    e0 = mark()
-    kc, _ = ops.compress_keys(k_full, cu(0, n), kernel_size=cfg.kernel_size,
-                              kernel_stride=cfg.kernel_stride, lengths=[n])
-    e1 = mark()
+    k, v = k.contiguous(), v.contiguous()
+    k_full = torch.empty(n, g, d, dtype=k.dtype, device=dev)
+    v_full = torch.empty_like(k_full)
+    k_late = torch.empty(half, g, d, dtype=k.dtype, device=dev)
+    v_late = torch.empty_like(k_late)
     pages = (n + cfg.block_size - 1) // cfg.block_size
     take = min(cfg.topk, pages)
     weights = selector.kernel_weights()
-    ks = ops.project_atom_keys(kc, weights.wk_t)
-    idxs = []
-    for i, (start, length) in enumerate(chunks):
-        idxs.append(ops.select_pages_chunk(
+
+    e_g0 = mark()
+    dist.all_gather_into_tensor(k_full[:half], k[:c], group=group)
+    dist.all_gather_into_tensor(v_full[:half], v[:c], group=group)
+    comm.wait_stream(compute)
+    with torch.cuda.stream(comm):
+        dist.all_gather_into_tensor(k_late, k[c:], group=group)
+        dist.all_gather_into_tensor(v_late, v[c:], group=group)
+    for t in (k, v, k_late, v_late):
+        t.record_stream(comm)
+
+    def chunk_work(i, kc_len):
+        """Compress K[:kc_len], select and attend query chunk i."""
+        start, length = chunks[i]
+        e0 = mark()
+        kc, _ = ops.compress_keys(k_full[:kc_len], cu(0, kc_len), kernel_size=cfg.kernel_size,
+                                  kernel_stride=cfg.kernel_stride, lengths=[kc_len])
+        e1 = mark()
+        ks = ops.project_atom_keys(kc, weights.wk_t)
+        idx = ops.select_pages_chunk(
             q[i * c:(i + 1) * c], weights, ks, q_position=start, seq_len=n, take=take,
             init_blocks=cfg.init_blocks, local_blocks=cfg.local_blocks,
-            block_size=cfg.block_size, kernel_stride=cfg.kernel_stride))
-    e2 = mark()
+            block_size=cfg.block_size, kernel_stride=cfg.kernel_stride)
+        e2 = mark()
+        ops.sparse_attn(q[i * c:(i + 1) * c], k_full, v_full, cu(0, length),
+                        cu(0, start + length), length, start + length, idx, causal=True,
+                        out=attn[i * c:(i + 1) * c])
+        e3 = mark()
+        if timers is not None:
+            timers.extend([("compress", e0, e1), ("select", e1, e2), ("attn", e2, e3)])
+        return idx
+
     attn = torch.empty_like(q)
-    for i, (start, length) in enumerate(chunks):
-        ops.sparse_attn(q[i * c:(i + 1) * c], k_full, v_full, cu(0, length), cu(0, start + length),
-                        length, start + length, idxs[i], causal=True, out=attn[i * c:(i + 1) * c])
-    e3 = mark()
+    e_g1 = mark()
     if timers is not None:
-        timers.extend([("gather", e_g, e0), ("compress", e0, e1), ("select", e1, e2),
-                       ("attn", e2, e3)])
+        timers.append(("gather", e_g0, e_g1))
+    idx0 = chunk_work(0, half)
+    e_w0 = mark()
+    compute.wait_stream(comm)
+    # Rank r's late chunk is sequence chunk 2W-1-r: reverse the rank order.
+    k_full[half:].view(world, c, g, d).copy_(k_late.view(world, c, g, d).flip(0))
+    v_full[half:].view(world, c, g, d).copy_(v_late.view(world, c, g, d).flip(0))
+    e_w1 = mark()
+    if timers is not None:
+        timers.append(("gather", e_w0, e_w1))
+    idx1 = chunk_work(1, n)
     if key_counts is not None:
         positions = local_positions(n, world, rank, device=dev)
         total = 0
-        for i, (start, length) in enumerate(chunks):
-            total += count_attended_keys(idxs[i], None, cfg.block_size,
+        for i, idx in enumerate((idx0, idx1)):
+            total += count_attended_keys(idx, None, cfg.block_size,
                                          positions=positions[i * c:(i + 1) * c])
         key_counts.append(total)
     return attn

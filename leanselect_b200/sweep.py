@@ -102,8 +102,11 @@ def run_length(n: int, reps: int, device: torch.device, dist=None, seed: int = 0
         b.record()
         torch.cuda.synchronize()
         totals.append(a.elapsed_time(b))
+        spans = {s: 0.0 for s in STAGES}
         for name, e0, e1 in timers:
-            per_stage[name].append(e0.elapsed_time(e1))
+            spans[name] += e0.elapsed_time(e1)  # a stage may run as several spans
+        for name, ms in spans.items():
+            per_stage[name].append(ms)
     ops.check_status(device)
     ms = {s: (statistics.median(v) if v else 0.0) for s, v in per_stage.items()}
     ms["total"] = statistics.median(totals)
