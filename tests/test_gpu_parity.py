@@ -385,8 +385,13 @@ def test_cpu_tensors_are_rejected():
 
 
 def test_select_pages_exact_ties_pick_lowest_pages():
-    """All scores equal (zero head mix): the lowest candidate pages win, as in the oracle."""
-    lens = [3000, 1000]
+    """All scores equal (zero head mix): the lowest candidate pages win, as in the oracle.
+
+    The 20000-token sequence has rows of up to 310 candidates, past the
+    per-warp buffer, where the sampled cut keeps every candidate and the
+    whole-row radix takes over.
+    """
+    lens = [3000, 1000, 20000]
     inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
                               router_dim=32, hot_pages=2, seed=81, bf16=True)
     inp.params.head_mix[:] = 0.0
