@@ -135,3 +135,36 @@ def test_reference_budget_mapping():
     cfg = lsb.LayerConfig()
     assert (cfg.topk, cfg.local_blocks, cfg.init_blocks) == (67, 2, 1)
     assert lsb.ops.atom_count(31) == 0 and lsb.ops.atom_count(32768) == 2047
+
+
+def test_uniform_and_atom_score_entry_points_validate_on_host():
+    lib = _native.load()
+    fake = ctypes.c_void_p(1 << 20)
+    # 2 groups x (16 heads x 128 x 128 bf16 weights, padded) + Ks + selection workspace
+    need = lib.ls_uniform_select_workspace_bytes(1000, 61, 32, 2, 1000)
+    assert need == 32 * 128 * 128 * 2 + (2 * 61 * 128 * 2 + 255) // 256 * 256 + 2 * 1000 * 16 * 4
+    rc = lib.ls_uniform_select_pages(fake, fake, fake, fake, 1, 1000, 1000, 61, 32, 2, 128, 35, 1,
+                                     2, 64, 16, 0.0, fake, fake, need - 1, None, None)
+    assert rc == _native.LS_ERR_INVALID_ARGUMENT and b"workspace" in lib.ls_last_error()
+    rc = lib.ls_uniform_select_pages(fake, fake, fake, fake, 1, 1000, 1000, 61, 32, 2, 64, 35, 1,
+                                     2, 64, 16, 0.0, fake, fake, need, None, None)
+    assert rc == _native.LS_ERR_UNSUPPORTED  # head_dim 64
+    rc = lib.ls_uniform_select_pages(None, fake, fake, fake, 1, 1000, 1000, 61, 32, 2, 128, 35, 1,
+                                     2, 64, 16, 0.0, fake, fake, need, None, None)
+    assert rc == _native.LS_ERR_INVALID_ARGUMENT
+    rc = lib.ls_atom_scores(fake, fake, fake, fake, fake, 1, 1000, 1000, 61, 32, 2, 128, 64, 61,
+                            fake, None, None)
+    assert rc == _native.LS_ERR_UNSUPPORTED  # selector width 64
+    rc = lib.ls_sparse_attn_gather_only(fake, fake, fake, fake, fake, 1, 64, 64, 64, 64, 24, 2, 128,
+                                        fake, 4, 64, 1, None, None)
+    assert rc == _native.LS_ERR_UNSUPPORTED  # 12 heads per group
+
+
+def test_noalloc_rejects_oversize_requests_on_host():
+    lib = _native.load()
+    fake = ctypes.c_void_p(1 << 20)
+    # one 2-group sequence of 64K tokens needs 2 x 65536 x 1024 x 4 bytes = 512 MiB > 16 MiB
+    rc = lib.ls_select_pages_noalloc(fake, fake, fake, fake, fake, 1, 65536, 65536, 4095, 32, 2,
+                                     128, 128, 67, 1, 2, 64, 16, fake, None, None)
+    assert rc == _native.LS_ERR_UNSUPPORTED
+    assert b"scratch" in lib.ls_last_error()
