@@ -82,7 +82,9 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_sequence_parallel_single_rank_matches_single_device():
+@pytest.mark.parametrize("n", [8192, 4096])
+def test_sequence_parallel_single_rank_matches_single_device(n):
+    """Bit-equal with and without the overlapped late gather (4096- and 2048-token chunks)."""
     import torch.distributed as dist
     from leanselect_b200.parallel import SequenceParallelRunner
 
@@ -91,7 +93,6 @@ def test_sequence_parallel_single_rank_matches_single_device():
     dist.init_process_group("nccl", rank=0, world_size=1, device_id=DEV)
     try:
         shape = small_shape()
-        n = 8192
         ids = torch.randint(0, 1000, (n,), device=DEV, generator=torch.Generator(device=DEV).manual_seed(4))
         sp = SequenceParallelRunner(shape, DEV, seed=5)
         ref = PrefillModel(shape, DEV, seed=5)

@@ -62,12 +62,13 @@ def _worker(rank, world, port, n, queue):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
-def test_sequence_parallel_matches_single_device(world):
+@pytest.mark.parametrize("world,n", [(2, 16384), (2, 8192)])
+def test_sequence_parallel_matches_single_device(world, n):
+    """4096-token chunks overlap the late K/V gather with the early chunk;
+    2048-token chunks gather everything first."""
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    n = 16384
     procs = [ctx.Process(target=_worker, args=(r, world, port, n, queue)) for r in range(world)]
     for p in procs:
         p.start()
