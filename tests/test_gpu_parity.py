@@ -434,9 +434,12 @@ def test_per_sequence_budgets_match_oracle():
     _attn_check(out, None, ref, None)
 
 
-def test_nosa_atom_scores_match_oracle():
-    """Raw atom scores for NOSA's precomputed-score path (nosa.py:1822-1853)."""
-    lens = [900, 20, 1333]
+@pytest.mark.parametrize("lens", [[900, 20, 1333], [1040, 300]])
+def test_nosa_atom_scores_match_oracle(lens):
+    """Raw atom scores for NOSA's precomputed-score path (nosa.py:1822-1853).
+
+    82 atoms per row take the kernel's scalar stores, 64 its 16-byte stores.
+    """
     inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
                               router_dim=32, hot_pages=3, seed=97, bf16=True)
     kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
