@@ -93,3 +93,11 @@ def test_config4_budget_rule():
     assert config4_budget(8192) == 12 + 3          # 128 pages -> 12
     assert config4_budget(32768) == 51 + 3         # 512 pages -> 51
     assert config4_budget(131072) == 64 + 3        # capped at 64
+
+
+def test_config4_batch_lengths_are_seeded_and_in_range():
+    from leanselect_b200.batched import batch_lengths
+    a, b = batch_lengths(64, 0), batch_lengths(64, 0)
+    assert a == b and len(a) == 64
+    assert all(8192 <= n <= 32768 for n in a)
+    assert batch_lengths(64, 1) != a
