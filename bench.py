@@ -197,6 +197,41 @@ def run_reference(args):
 # GPU arm
 # ---------------------------------------------------------------------------
 
+def stage_roofline(shape, n: int, stage_ms: dict, attn_flops: float, pk: dict) -> dict:
+    """Algorithmic work of each hot-path stage of one layer against its bound.
+
+    Single sequence of ``n`` tokens; G KV groups, H heads, D = F = 128, page
+    64, atoms A = (n - 32) // 16 + 1, pages P.  Compression moves K in and Kc
+    out (HBM).  Selection computes the query projection (2 n H D F flops) and
+    the causally reachable atom scores (about G F n A flops), and moves Q in,
+    the pooled-score rows out and back (about G n P / 2 floats each way) and
+    the page lists out (HBM).  Attention is the kernel of ``roofline``.  The
+    stage times are the bench's own per-layer CUDA-event spans.
+    """
+    g, h, d = shape.num_kv_heads, shape.num_heads, shape.head_dim
+    f = shape.router_heads * shape.router_dim
+    atoms = (n - 32) // 16 + 1 if n >= 32 else 0
+    pages = (n + 63) // 64
+    take = min(shape.sparse.topk, pages)
+    hbm = pk["hbm_gbs"] * 1e9
+    tensor = pk["bf16_tflops_sustained"] * 1e12
+    comp_bytes = (n + atoms) * g * d * 2
+    sel_flops = 2.0 * n * h * d * f + g * f * n * atoms
+    sel_bytes = n * h * d * 2 + 2 * (g * n * pages / 2) * 4 + g * n * take * 4
+    t_c, t_s, t_a = (stage_ms[k] / 1e3 for k in ("compress", "select", "attn"))
+    return {
+        "compress": {"bound": "hbm", "bytes": comp_bytes, "achieved_gbs": comp_bytes / t_c / 1e9,
+                     "frac": comp_bytes / t_c / hbm},
+        "select": {"flops": sel_flops, "bytes": sel_bytes,
+                   "achieved_tflops": sel_flops / t_s / 1e12, "tensor_frac": sel_flops / t_s / tensor,
+                   "achieved_gbs": sel_bytes / t_s / 1e9, "hbm_frac": sel_bytes / t_s / hbm},
+        "select_attn": {"flops": sel_flops + attn_flops,
+                        "achieved_tflops": (sel_flops + attn_flops) / (t_s + t_a) / 1e12,
+                        "tensor_frac": (sel_flops + attn_flops) / (t_s + t_a) / tensor},
+        "peaks": "MEASURED_PEAKS.json hbm_gbs and bf16_tflops_sustained",
+    }
+
+
 def gather_roofline(runner, ids_dev, lengths, keys_last_layer: int, reps: int = 3) -> dict:
     """The attention kernel against its own data movement (measured roofline).
 
@@ -379,6 +414,7 @@ def run_ours(args):
     }
     if world == 1:
         line["roofline"]["l2_gather"] = gather_roofline(runner, ids_dev, lengths, key_counts[-1])
+        line["stage_roofline"] = stage_roofline(shape, n, stage_ms, flops_per_layer, pk)
     if rank == 0 and world == 1:
         cpu = CpuHotPath(n, args.layers, args.cpu_rows, args.seed)
         line["cpu_baseline"] = cpu.describe(cpu.step())
