@@ -583,3 +583,25 @@ def test_torch_custom_ops_match_fake_shapes():
     torch.library.opcheck(torch.ops.leanselect_b200.select_pages.default,
                           (q, w.wq_t, ks, cu, cu_c, max(lens), 9, 1, 2), test_utils=checks)
     assert ops.check_status(DEV) == 0
+
+
+def test_custom_op_traces_under_torch_compile():
+    """The fake shapes carry the op through a traced graph (aot_eager, full graph)."""
+    import leanselect_b200.torch_ops  # noqa: F401
+    lens = [500, 300]
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=2, seed=14, bf16=True)
+    q, k, v = to_dev(inp.q), to_dev(inp.k), to_dev(inp.v)
+    cu = cu_dev(inp.cu_seqlens)
+    rng = np.random.default_rng(2)
+    idx = to_dev(rng.integers(-1, 8, size=(2, sum(lens), 6)).astype(np.int32), torch.int32)
+
+    def layer(q, k, v, cu, idx):
+        out, lse = torch.ops.leanselect_b200.sparse_attn(q, k, v, cu, cu, 500, 500, idx, 0.0, True)
+        return out.float() * 2.0, lse
+
+    torch._dynamo.reset()
+    compiled = torch.compile(layer, backend="aot_eager", fullgraph=True)
+    got_out, got_lse = compiled(q, k, v, cu, idx)
+    want_out, want_lse = layer(q, k, v, cu, idx)
+    assert torch.equal(got_out, want_out) and torch.equal(got_lse, want_lse)
