@@ -62,10 +62,12 @@ struct Barriers {
   int abort_flag;
 };
 
+constexpr int kStoreStageBytes = 4 * 32 * 8 * 4;  // per epilogue warp: 32 rows x 8 pages fp32
+
 __host__ __device__ constexpr size_t smem_bytes(int mode) {
   return 1024  // alignment slack
          + static_cast<size_t>(kStages) * kStageBytes + (mode == kModeProject ? 0 : kQsBytes) +
-         sizeof(Barriers);
+         sizeof(Barriers) + 16 + kStoreStageBytes;
 }
 
 struct TileInfo {
@@ -162,6 +164,10 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
   uint8_t* qs_smem = stages + kStages * kStageBytes;
   Barriers* bars =
       reinterpret_cast<Barriers*>(qs_smem + (MODE == kModeProject ? 0 : kQsBytes));
+  // Page-score staging: each epilogue warp turns its 32 rows x 8 pages into
+  // row-contiguous 32-byte stores.
+  float* store_stage = reinterpret_cast<float*>(
+      (reinterpret_cast<uintptr_t>(bars + 1) + 15) & ~static_cast<uintptr_t>(15));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -391,14 +397,34 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
                   if (p0 + i >= ti.pages) pg[i] = -INFINITY;
               }
               if ((args.max_pages & 7) == 0) {
-                // Workspace rows (select mode) are padded to 8 pages: 32-byte stores.
-                *reinterpret_cast<float4*>(out_row + p0) = make_float4(pg[0], pg[1], pg[2], pg[3]);
-                *reinterpret_cast<float4*>(out_row + p0 + 4) = make_float4(pg[4], pg[5], pg[6], pg[7]);
+                // Rows padded to 8 pages (the select workspace): stage the warp's
+                // 32 x 8 block in shared memory and write it back as 32-byte row
+                // segments, two lanes per row.
+                float* st = store_stage + quad * 256;
+                *reinterpret_cast<float4*>(st + lane * 8) = make_float4(pg[0], pg[1], pg[2], pg[3]);
+                *reinterpret_cast<float4*>(st + lane * 8 + 4) = make_float4(pg[4], pg[5], pg[6], pg[7]);
               } else {
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
                   if (p0 + i < args.max_pages) out_row[p0 + i] = pg[i];
               }
+            }
+            if (p0 < args.max_pages && (args.max_pages & 7) == 0) {
+              __syncwarp();
+              const float* st = store_stage + quad * 256;
+              float* wbase = (MODE == kModeScore ? args.page_scores : args.workspace) +
+                             (static_cast<int64_t>(ti.g) * args.total_q + ti.q0 + ti.row0 +
+                              quad * 32) * args.max_pages + p0;
+#pragma unroll
+              for (int i = 0; i < 2; ++i) {
+                const int c = lane + 32 * i;  // row c / 2, half c % 2
+                const int r = c >> 1;
+                if (quad * 32 + r < ti.rows)
+                  *reinterpret_cast<float4*>(wbase + static_cast<int64_t>(r) * args.max_pages +
+                                             4 * (c & 1)) =
+                      *reinterpret_cast<const float4*>(st + r * 8 + 4 * (c & 1));
+              }
+              __syncwarp();
             }
           }
         }
