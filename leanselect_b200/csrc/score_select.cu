@@ -470,7 +470,6 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
 // ---------------------------------------------------------------------------
 
 constexpr int kTopkWarps = 8;
-constexpr int kDirectMax = 256;      // rows with at most this many candidates: radix on the row
 constexpr int kBufCap = 256;         // per-warp candidate buffer (8 blocks of 8 warps fit an SM)
 
 // Order-preserving map of fp32 to uint32; -inf and NaN map to 0 (never picked).
