@@ -408,7 +408,7 @@ def run_ours(args):
             # this command at 131072 tokens: mean of 24 launches captured in one
             # ncu pass (`--metrics gpu__time_duration.sum,dram__bytes_read.sum,
             # dram__bytes_write.sum`, 4 layers).
-            "traffic": 6858.6e6 + 1071.0e6,
+            "traffic": 6650.1e6 + 1070.9e6,
         },
         "clocks": clocks.summary(),
     }
