@@ -1,6 +1,7 @@
 """Sequence-length sweep of one hot-path layer.
 
     python -m leanselect_b200.sweep [--lengths 32768,65536,131072,262144,524288] [--reps 3]
+                                    [--method leanselect|uniform]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
         -m leanselect_b200.sweep ...            # sequence-parallel over N GPUs
 
@@ -66,10 +67,13 @@ def make_selector(device: torch.device, seed: int = 0, num_heads: int = 32,
     return sel.to(device)
 
 
-def run_length(n: int, reps: int, device: torch.device, dist=None, seed: int = 0) -> dict:
+def run_length(n: int, reps: int, device: torch.device, dist=None, seed: int = 0,
+               method: str = "leanselect") -> dict:
     world = dist.get_world_size() if dist is not None else 1
     rank = dist.get_rank() if dist is not None else 0
-    cfg = LayerConfig(topk=67)
+    if method != "leanselect" and world > 1:
+        raise ValueError("the sequence-parallel layer serves the LeanSelect method only")
+    cfg = LayerConfig(topk=67, selection_method=method)
     q, k, v = config1_layer(n, device, seed)
     sel = make_selector(device, seed)
     if world > 1:
@@ -115,7 +119,7 @@ def run_length(n: int, reps: int, device: torch.device, dist=None, seed: int = 0
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = dict(zip((*STAGES, "total"), t.tolist()))
     return {"workload": "BASELINE config 3: config-1 layer (bf16, 32/2 heads, T=67)",
-            "seq_len": n, "n_gpus": world, "reps": reps, "ms": ms,
+            "method": method, "seq_len": n, "n_gpus": world, "reps": reps, "ms": ms,
             "tokens_per_s": n / (ms["total"] / 1e3),
             "parallelism": f"sp{world}" if world > 1 else "single"}
 
@@ -125,6 +129,8 @@ def main(argv=None) -> int:
     ap.add_argument("--lengths", default="32768,65536,131072,262144,524288")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--method", choices=("leanselect", "uniform"), default="leanselect",
+                    help="selection method (uniform: the mean-query ablation, one GPU)")
     args = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -139,7 +145,7 @@ def main(argv=None) -> int:
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
     try:
         for n in (int(x) for x in args.lengths.split(",")):
-            line = run_length(n, args.reps, device, dist, args.seed)
+            line = run_length(n, args.reps, device, dist, args.seed, args.method)
             if dist is None or dist.get_rank() == 0:
                 print(json.dumps(line), flush=True)
             torch.cuda.empty_cache()
