@@ -1,6 +1,6 @@
 """Benchmark: 128K-token prefill of a random-init MiniCPM4.1-8B-shaped model.
 
-The metric (BASELINE.json) is prefill tokens/s at 128K for the 8B shape, with
+The metric is prefill tokens/s at 128K for the 8B shape, with
 LeanSelect selection and block-sparse attention on every layer; the hot path
 (compress -> select -> sparse attention) is also reported as ms per layer.
 

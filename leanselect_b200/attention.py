@@ -168,7 +168,7 @@ class LayerConfig:
     local_blocks: int = 2
     selection_method: str = "leanselect"
     # Optional per-sequence budget: maps a sequence length to its total page
-    # count T (e.g. min(64, pages // 10) + sink + local).
+    # count T (e.g. benchmark config 4: min(64, pages // 10) + sink + local).
     # The reference takes one T per packed call (minicpm.py:3104), so such a
     # batch is selected sequence by sequence and padded to the largest T.
     per_sequence_topk: Callable[[int], int] | None = None
@@ -176,7 +176,7 @@ class LayerConfig:
 
 def config4_budget(seq_len: int, block_size: int = 64, init_blocks: int = 1,
                    local_blocks: int = 2) -> int:
-    """BASELINE config 4 budget: min(64, floor(0.1 * pages)) + sink + local pages."""
+    """benchmark config 4 budget: min(64, floor(0.1 * pages)) + sink + local pages."""
     pages = (int(seq_len) + block_size - 1) // block_size
     return min(64, pages // 10) + init_blocks + local_blocks
 

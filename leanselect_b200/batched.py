@@ -1,4 +1,4 @@
-"""Batched small-model prefill, data-parallel.
+"""Batched small-model prefill, data-parallel (benchmark config 4).
 
     python -m leanselect_b200.batched [--sequences 64] [--steps 2] [--warmup 1]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
@@ -91,7 +91,7 @@ def main(argv=None) -> int:
         if rank == 0:
             total = sum(lengths)
             print(json.dumps({
-                "metric": "batched prefill tokens/sec (BASELINE config 4)",
+                "metric": "batched prefill tokens/sec (benchmark config 4)",
                 "value": total / (ms_step / 1e3), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
                 "scaling": "strong", "dtype": "bf16",

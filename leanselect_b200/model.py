@@ -56,7 +56,7 @@ class MiniCPMShape:
 
     @classmethod
     def small_24l(cls, **kw) -> "MiniCPMShape":
-        """24 layers, hidden 2048, 16/2 heads, head_dim 128."""
+        """benchmark config 4: 24 layers, hidden 2048, 16/2 heads, head_dim 128."""
         base = dict(hidden_size=2048, intermediate_size=8192, num_layers=24, num_heads=16,
                     num_kv_heads=2, max_position=32768, original_max_position=32768,
                     router_heads=4, router_dim=32)

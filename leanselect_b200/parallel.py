@@ -218,7 +218,7 @@ def sequence_parallel_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s
 
 
 class DataParallelRunner:
-    """Batched prefill: sequences sharded over ranks, no collectives.
+    """Batched prefill (benchmark config 4): sequences sharded over ranks, no collectives.
 
     Every rank holds the whole model (same seed), takes its LPT shard of the
     batch, and prefills it as one packed varlen batch; ranks never exchange

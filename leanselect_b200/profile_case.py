@@ -2,7 +2,7 @@
 
     python -m leanselect_b200.profile_case [--seq-len 32768] [--topk 67] [--repeat 1]
 
-Builds BASELINE config-1-shaped inputs (32 query / 2 KV heads, head_dim 128,
+Builds benchmark config-1-shaped inputs (32 query / 2 KV heads, head_dim 128,
 N(0,1) q/k/v, selector with a 32x4 router) on ``cuda:0`` and runs
 compression -> key projection -> fused scoring + top-k -> sparse attention
 ``--repeat`` times, then checks the device status word.  Meant to be run

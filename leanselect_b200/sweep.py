@@ -1,11 +1,11 @@
-"""Sequence-length sweep of one hot-path layer.
+"""Sequence-length sweep of one hot-path layer (benchmark config 3).
 
     python -m leanselect_b200.sweep [--lengths 32768,65536,131072,262144,524288] [--reps 3]
                                     [--method leanselect|uniform]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
         -m leanselect_b200.sweep ...            # sequence-parallel over N GPUs
 
-One BASELINE config-1 layer (bf16, 32 query / 2 KV heads, head_dim 128,
+One benchmark config-1 layer (bf16, 32 query / 2 KV heads, head_dim 128,
 budget 64 pages + sink + 2 local pages of 64 tokens) at each length, with
 the config-0/1 input distribution: N(0,1) q/k/v, 24 hot pages per KV head
 whose keys (and every query) are shifted by 0.5*u, selector head mix
@@ -38,7 +38,7 @@ STAGES = ("gather", "compress", "select", "attn")
 def config1_layer(n: int, device: torch.device, seed: int = 0, num_heads: int = 32,
                   num_kv_heads: int = 2, head_dim: int = 128, hot_pages: int = 24,
                   hot_shift: float = 0.5):
-    """BASELINE config-0/1 distribution for one sequence of ``n`` tokens, on ``device``."""
+    """benchmark config-0/1 distribution for one sequence of ``n`` tokens, on ``device``."""
     g = torch.Generator(device=device).manual_seed(seed)
     q = torch.randn(n, num_heads, head_dim, device=device, generator=g)
     k = torch.randn(n, num_kv_heads, head_dim, device=device, generator=g)
@@ -118,7 +118,7 @@ def run_length(n: int, reps: int, device: torch.device, dist=None, seed: int = 0
         t = torch.tensor([ms[s] for s in (*STAGES, "total")], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = dict(zip((*STAGES, "total"), t.tolist()))
-    return {"workload": "BASELINE config 3: config-1 layer (bf16, 32/2 heads, T=67)",
+    return {"workload": "benchmark config 3: config-1 layer (bf16, 32/2 heads, T=67)",
             "method": method, "seq_len": n, "n_gpus": world, "reps": reps, "ms": ms,
             "tokens_per_s": n / (ms["total"] / 1e3),
             "parallelism": f"sp{world}" if world > 1 else "single"}

@@ -13,7 +13,7 @@ Numeric policies
 ----------------
 ``policy="fp32"``
     Everything in fp32 semantics, like the reference run on fp32 tensors
-    Contractions accumulate in float64 and round to
+    (benchmark config 0).  Contractions accumulate in float64 and round to
     float32, which is at least as accurate as torch's fp32 einsum.
 ``policy="bf16"``
     The rounding points of the reference's bf16 model path:
@@ -510,7 +510,7 @@ def sparse_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, cu_seqlens_q: 
 
 
 # ----------------------------------------------------------------------------
-# Seeded synthetic inputs
+# Seeded synthetic inputs (benchmark configs)
 # ----------------------------------------------------------------------------
 
 @dataclass
@@ -530,7 +530,7 @@ def selector_params(num_heads: int, num_kv_heads: int, head_dim: int, router_hea
     ``q_proj``/``k_proj`` follow ``reset_parameters`` (selector.py:112-137):
     an orthonormal frame from a QR of a Gaussian matrix, scaled by
     ``head_dim**-0.25``, reshaped to ``[R, D, r]``.  ``head_mix`` is a seeded
-    ``N(0, 1/R)`` matrix ("32x32 N(0, 1/32) per group"
+    ``N(0, 1/R)`` matrix (benchmark config 0: "32x32 N(0, 1/32) per group"
     with ``router_heads = 32``) and ``kv_head_mix = 1``.
     """
     width = router_heads * router_dim
@@ -551,7 +551,7 @@ def synthetic_layer(seq_lens, *, num_heads: int = 32, num_kv_heads: int = 2, hea
                     router_heads: int = 32, router_dim: int = 4, hot_pages: int = 24,
                     hot_shift: float = 0.5, block_size: int = 64, seed: int = 0,
                     bf16: bool = False) -> LayerInputs:
-    """BASELINE config-0/1 generator for a packed batch of sequences.
+    """benchmark config-0/1 generator for a packed batch of sequences.
 
     Q, K, V ~ N(0, 1).  In each sequence and KV head, ``hot_pages`` distinct
     random pages have their keys shifted by ``hot_shift * u``; every query
@@ -596,7 +596,7 @@ def select_for_queries(q_rows: np.ndarray, positions, seq_len: int, kc: np.ndarr
     ``q_rows [R, H, D]`` are the queries at ``positions`` (relative, length
     ``R``); ``kc [A, G, D]`` are all atoms of the sequence.  Same math as
     :func:`lightweight_compressed_attention` restricted to those rows, so the
-    long BASELINE configurations can be checked (and timed on the CPU) on a
+    long benchmark configurations can be checked (and timed on the CPU) on a
     sample without scoring every row.  ``take`` is the output width.
     """
     positions = np.asarray(positions, dtype=np.int64)

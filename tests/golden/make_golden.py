@@ -173,7 +173,7 @@ def selection_cases():
 
 
 def config0_case():
-    """BASELINE config 0 (N=8192, 32/2 heads, D=128, T=35, fp32) via the reference.
+    """benchmark config 0 (N=8192, 32/2 heads, D=128, T=35, fp32) via the reference.
 
     The inputs are regenerated from the seed by the oracle generator; the
     fixture keeps their SHA-256 so a changed random stream fails loudly.

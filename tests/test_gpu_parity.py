@@ -225,7 +225,7 @@ def test_select_pages_matches_oracle(case):
 
 
 def test_select_config1_rows():
-    """BASELINE config 1 (N=32768, 32/2 heads, T=67, bf16) on a row sample."""
+    """benchmark config 1 (N=32768, 32/2 heads, T=67, bf16) on a row sample."""
     n = 32768
     inp = ora.synthetic_layer([n], seed=1, bf16=True)
     kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
@@ -348,7 +348,7 @@ def test_sparse_attention_flags_out_of_range_pages():
 
 
 def test_prefill_layer_config1_rows():
-    """Whole hot path at BASELINE config-1 size, checked on sampled rows."""
+    """Whole hot path at benchmark config-1 size, checked on sampled rows."""
     n = 32768
     inp = ora.synthetic_layer([n], seed=2, bf16=True)
     sel = selector_for(inp.params)
@@ -407,7 +407,7 @@ def test_select_pages_exact_ties_pick_lowest_pages():
 
 
 def test_per_sequence_budgets_match_oracle():
-    """BASELINE config-4 style budgets: each sequence selected with its own T."""
+    """benchmark config-4 style budgets: each sequence selected with its own T."""
     from leanselect_b200.attention import config4_budget
 
     lens = [1300, 2700, 640]
@@ -521,7 +521,7 @@ def test_uniform_through_minicpm_dispatch():
 
 
 def test_uniform_config1_rows():
-    """BASELINE config-1 shape (N=32768, 32/2 heads, T=67) on a row sample."""
+    """benchmark config-1 shape (N=32768, 32/2 heads, T=67) on a row sample."""
     n = 32768
     inp = ora.synthetic_layer([n], seed=7, bf16=True)
     kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")

@@ -130,7 +130,7 @@ def test_selection_matches_reference(name):
 
 
 def test_config0_selection_matches_reference():
-    """BASELINE config 0 (fp32, N=8192, T=35) against the reference's topk_idx."""
+    """benchmark config 0 (fp32, N=8192, T=35) against the reference's topk_idx."""
     g = load("config0.npz")
     inputs = ora.synthetic_layer([8192], seed=int(g["seed"]))
     assert digest(inputs.q, inputs.k, inputs.v) == str(g["input_digest"])

@@ -78,7 +78,7 @@ def test_lpt_shards_cover_every_sequence_once_and_balance():
 
     import numpy as np
     rng = np.random.default_rng(0)
-    lengths = rng.integers(8192, 32769, 64).tolist()
+    lengths = rng.integers(8192, 32769, 64).tolist()   # benchmark config 4
     shards = lpt_shards(lengths, 8)
     flat = sorted(i for s in shards for i in s)
     assert flat == list(range(64))
