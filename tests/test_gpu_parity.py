@@ -331,6 +331,32 @@ def test_decode_step_through_sparse_forward_contract():
     assert ops.check_status(DEV) == 0
 
 
+def test_sparse_attention_query_chunk_against_key_prefix():
+    """Causal, fewer queries than keys: the queries are the last rows of each
+    sequence's keys (bottom-right alignment), the form a sequence-parallel rank
+    uses for its late chunk.  Page lists drawn over the whole key range."""
+    k_lens = [2000, 700, 4096]
+    q_lens = [333, 700, 1000]
+    heads, groups = 32, 2
+    inp = ora.synthetic_layer(k_lens, num_heads=heads, num_kv_heads=groups, head_dim=128,
+                              router_heads=4, router_dim=32, hot_pages=2, seed=83, bf16=True)
+    cu_k = inp.cu_seqlens
+    rows = np.concatenate([np.arange(cu_k[b + 1] - nq, cu_k[b + 1]) for b, nq in enumerate(q_lens)])
+    q = inp.q[rows]
+    cu_q = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
+    rng = np.random.default_rng(12)
+    idx = np.full((groups, len(rows), 20), -1, dtype=np.int32)
+    for b, (nq, nk) in enumerate(zip(q_lens, k_lens)):
+        pages = (nk + 63) // 64
+        idx[:, cu_q[b]:cu_q[b + 1]] = rng.integers(-1, pages, size=(groups, nq, 20))
+    out, lse = ops.sparse_attn(to_dev(q), to_dev(inp.k), to_dev(inp.v), cu_dev(cu_q),
+                               cu_dev(cu_k), max(q_lens), max(k_lens), to_dev(idx, torch.int32),
+                               return_lse=True)
+    want, want_lse = ora.sparse_attention(q, inp.k, inp.v, cu_q, cu_k, idx)
+    _attn_check(out, lse, want, want_lse)
+    assert ops.check_status(DEV) == 0
+
+
 def test_sparse_attention_flags_out_of_range_pages():
     lens = [200]
     inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
