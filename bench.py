@@ -168,6 +168,21 @@ class CpuHotPath:
         }
 
 
+def workload_config(n: int, layers: int, world: int) -> dict:
+    """The ``config`` object of both arms' JSON lines (the same workload)."""
+    from leanselect_b200.model import MiniCPMShape
+
+    shape = MiniCPMShape.minicpm41_8b(num_layers=layers, max_position=max(n, 65536))
+    return {
+        "workload": f"random-init MiniCPM4.1-8B-shaped prefill, {n} tokens, batch 1, "
+                    f"{layers} layers, LeanSelect T=67 (64 + sink + 2 local) pages of 64",
+        "seq_len": n, "layers": layers, "hidden": shape.hidden_size,
+        "heads": f"{shape.num_heads}/{shape.num_kv_heads}", "head_dim": shape.head_dim,
+        "parallelism": f"sp{world}" if world > 1 else "single",
+        "l2": "working set larger than L2 (16 GB of weights, >=1 GB activations per layer)",
+    }
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -182,9 +197,7 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": len(steps), "warmup": args.warmup,
         "ms_per_step": args.seq_len / value * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"MiniCPM4.1-8B-shaped prefill hot path, {args.seq_len} tokens, "
-                               f"{args.layers} layers, T=67 pages of 64",
-                   "seq_len": args.seq_len, "layers": args.layers},
+        "config": workload_config(args.seq_len, args.layers, args.gpus),
         "cpu_baseline": cpu.describe(value),
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -381,14 +394,7 @@ def run_ours(args):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (uniform random token ids, random-init weights)",
-        "config": {
-            "workload": f"random-init MiniCPM4.1-8B-shaped prefill, {n} tokens, batch 1, "
-                        f"{args.layers} layers, LeanSelect T=67 (64 + sink + 2 local) pages of 64",
-            "seq_len": n, "layers": args.layers, "hidden": shape.hidden_size,
-            "heads": f"{shape.num_heads}/{shape.num_kv_heads}", "head_dim": shape.head_dim,
-            "parallelism": f"sp{world}" if world > 1 else "single",
-            "l2": "working set larger than L2 (16 GB of weights, >=1 GB activations per layer)",
-        },
+        "config": workload_config(n, args.layers, world),
         "select_attn_ms_per_layer": stage_ms["select"] + attn_ms + stage_ms["compress"],
         "stage_ms_per_layer": stage_ms,
         "e2e": {"value": n / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": n * 8,
