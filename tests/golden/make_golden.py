@@ -279,6 +279,21 @@ def nosa_atom_score_cases():
         scores_bits=scores.view(torch.int16).numpy())
 
 
+def selector_init_cases():
+    """Default initialisation (``reset_parameters``, selector.py:112-137) under fixed seeds:
+    the reference test's shape, the benchmark's, and a router wider than head_dim."""
+    out = {}
+    shapes = [(8, 2, 8, 2, 4), (32, 2, 128, 4, 32), (8, 2, 16, 8, 4)]
+    for i, (h, g, d, rh, rd) in enumerate(shapes):
+        torch.manual_seed(100 + i)
+        sel = LeanSelectSelector(num_heads=h, num_kv_heads=g, head_dim=d, router_heads=rh,
+                                 router_dim=rd)
+        for name in ("head_mix", "kv_head_mix", "q_proj", "k_proj"):
+            out[f"{i}_{name}"] = getattr(sel, name).detach().numpy()
+        out[f"{i}_shape"] = np.array([h, g, d, rh, rd], dtype=np.int64)
+        out[f"{i}_seed"] = np.int64(100 + i)
+    np.savez_compressed(HERE / "selector_init.npz", **out)
+
 if __name__ == "__main__":
     torch.manual_seed(0)
     known_answers()
@@ -289,5 +304,6 @@ if __name__ == "__main__":
     bf16_selection_case()
     uniform_cases()
     nosa_atom_score_cases()
+    selector_init_cases()
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)

@@ -130,6 +130,48 @@ def test_selector_initialisation_matches_reference_rule():
     assert torch.equal(sel.q_proj, sel.k_proj)
 
 
+def test_selector_initialisation_is_bit_identical_to_reference():
+    """``tests/golden/selector_init.npz`` holds the reference selector's own
+    initial parameters under fixed seeds (narrow, benchmark and wide router)."""
+    import numpy as np
+
+    fixture = np.load(ROOT / "tests" / "golden" / "selector_init.npz")
+    for i in range(3):
+        h, g, d, rh, rd = (int(x) for x in fixture[f"{i}_shape"])
+        torch.manual_seed(int(fixture[f"{i}_seed"]))
+        sel = lsb.LeanSelectSelector(num_heads=h, num_kv_heads=g, head_dim=d, router_heads=rh,
+                                     router_dim=rd)
+        for name in ("head_mix", "kv_head_mix", "q_proj", "k_proj"):
+            assert np.array_equal(getattr(sel, name).detach().numpy(), fixture[f"{i}_{name}"]), \
+                (i, name)
+
+
+@pytest.mark.parametrize("shape", [(8, 2, 8, 2, 4), (32, 2, 128, 4, 32)])
+def test_full_width_initialisation_is_scaled_head_mean_dot(shape):
+    """The reference's known answer (test_core.py:59-65): at router width
+    R*r = head_dim the initial selector scores query n against atom a as the
+    group-mean query dotted with the key, over sqrt(head_dim).  Checked for
+    the reference test's shape and for the benchmark's (32/2 heads, D 128,
+    4 x 32 router), through the folded weights the kernels consume."""
+    import numpy as np
+
+    from oracle import leanselect_oracle as ora
+
+    h, g, d, rh, rd = shape
+    torch.manual_seed(11)
+    sel = lsb.LeanSelectSelector(num_heads=h, num_kv_heads=g, head_dim=d, router_heads=rh,
+                                 router_dim=rd)
+    params = ora.SelectorParams(*(getattr(sel, name).detach().numpy()
+                                  for name in ("head_mix", "kv_head_mix", "q_proj", "k_proj")))
+    rng = np.random.default_rng(4)
+    q = rng.standard_normal((3, h, d)).astype(np.float32)
+    k = rng.standard_normal((7, g, d)).astype(np.float32)
+    q_fused, kv_fused = ora.fold_weights(params)
+    actual = ora.atom_scores(ora.project_queries(q, q_fused, g), ora.project_atom_keys(k, kv_fused))
+    expected = np.einsum("ngd,agd->gna", q.reshape(3, g, h // g, d).mean(2), k) / np.sqrt(d)
+    np.testing.assert_allclose(actual, expected, atol=1e-5, rtol=1e-4)
+
+
 def test_reference_budget_mapping():
     """Budget arithmetic of load_model / the attention module (minicpm.py:1965-1966)."""
     cfg = lsb.LayerConfig()
