@@ -242,6 +242,55 @@ def test_select_config1_rows():
     assert not bad, bad[:5]
 
 
+def test_full_size_selection_properties_and_row_parity():
+    """The benchmark's sequence length (131072 tokens, T=67) on the config-1
+    input distribution.  Every row of both groups: the page count is
+    min(T, q_page + 1), pages ascend without repeats, -1 only at the tail,
+    nothing past the query's page (test_runtime.py:71-94 checks the same
+    visibility), the sink and the three local pages always present.  A row
+    sample then matches the oracle's selection and attention."""
+    from leanselect_b200.sweep import config1_layer, make_selector
+
+    n, T = 131072, 67
+    q, k, v = config1_layer(n, DEV, 5)
+    sel = make_selector(DEV, 5)
+    cu = torch.tensor([0, n], dtype=torch.int32, device=DEV)
+    w = sel.kernel_weights()
+    kc, cu_c = ops.compress_keys(k, cu, lengths=[n])
+    ks = ops.project_atom_keys(kc, w.wk_t)
+    idx = ops.select_pages(q, w, ks, cu, cu_c, n, take=T)
+    assert ops.check_status(DEV) == 0
+    assert idx.dtype == torch.int32 and idx.shape == (2, n, T)
+
+    qp = torch.arange(n, device=DEV) // 64
+    valid = idx >= 0
+    count = valid.sum(-1)
+    assert torch.equal(count, torch.clamp(qp + 1, max=T).expand(2, n))
+    assert torch.equal(valid, torch.arange(T, device=DEV) < count[..., None])
+    assert torch.all((idx[..., 1:] > idx[..., :-1]) | ~valid[..., 1:])
+    assert torch.all(idx <= qp[None, :, None])
+    assert torch.all((idx == 0).any(-1))
+    for back in (0, 1, 2):
+        assert torch.all((idx == (qp - back).clamp(min=0)[None, :, None]).any(-1))
+
+    rng = np.random.default_rng(2)
+    rows = np.unique(np.concatenate([[0, 63, 64, 4287, 4288], np.arange(n - 3, n),
+                                     rng.integers(0, n, 24)]))
+    params = ora.SelectorParams(*(getattr(sel, name).detach().float().cpu().numpy()
+                                  for name in ("head_mix", "kv_head_mix", "q_proj", "k_proj")))
+    q_rows = q[torch.from_numpy(rows).to(DEV)].float().cpu().numpy()
+    want = ora.select_for_queries(q_rows, rows, n, kc.float().cpu().numpy(), params, take=T)
+    got = idx.cpu().numpy()[:, rows]
+    bad = ora.selection_mismatches(got, want, rel_tol=1e-3)
+    assert not bad, bad[:5]
+
+    out = ops.sparse_attn(q, k, v, cu, cu, n, n, idx)
+    assert ops.check_status(DEV) == 0
+    ref = ora.attention_for_queries(q_rows, rows, k.float().cpu().numpy(),
+                                    v.float().cpu().numpy(), got)
+    _attn_check(out[torch.from_numpy(rows).to(DEV)], None, ref, None)
+
+
 # ---------------------------------------------------------------------------
 # a9: sparse attention
 # ---------------------------------------------------------------------------
