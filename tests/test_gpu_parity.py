@@ -242,6 +242,36 @@ def test_select_config1_rows():
     assert not bad, bad[:5]
 
 
+@pytest.mark.parametrize("method", ["leanselect", "uniform"])
+def test_packed_batch_equals_independent_sequences(method):
+    """Varlen packing changes nothing (the reference checks the same for its
+    uniform stage 1, test_core.py:213-232): the selection and the attention
+    of a packed batch equal, bit for bit, those of each sequence run alone.
+    The 20-token sequence has no atoms; the 64-token one a single page."""
+    lens = [1500, 64, 900, 2100, 20]
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=3, seed=93, bf16=True)
+    w = selector_for(inp.params).kernel_weights()
+    q, k, v = to_dev(inp.q), to_dev(inp.k), to_dev(inp.v)
+
+    def run(qq, kk, vv, cu, max_len, lengths):
+        kc, cu_c = ops.compress_keys(kk, cu, lengths=lengths)
+        if method == "uniform":
+            idx = ops.uniform_select_pages(qq, kc, cu, cu_c, max_len, take=20)
+        else:
+            ks = ops.project_atom_keys(kc, w.wk_t)
+            idx = ops.select_pages(qq, w, ks, cu, cu_c, max_len, take=20)
+        return idx, ops.sparse_attn(qq, kk, vv, cu, cu, max_len, max_len, idx)
+
+    idx_all, out_all = run(q, k, v, cu_dev(inp.cu_seqlens), max(lens), lens)
+    for b, n in enumerate(lens):
+        s = int(inp.cu_seqlens[b])
+        idx_b, out_b = run(q[s:s + n], k[s:s + n], v[s:s + n], cu_dev([0, n]), n, [n])
+        assert torch.equal(idx_all[:, s:s + n], idx_b), b
+        assert torch.equal(out_all[s:s + n], out_b), b
+    assert ops.check_status(DEV) == 0
+
+
 def test_full_size_selection_properties_and_row_parity():
     """The benchmark's sequence length (131072 tokens, T=67) on the config-1
     input distribution.  Every row of both groups: the page count is
