@@ -25,7 +25,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
-REFERENCE = os.environ.get("LEANSELECT_REFERENCE", "/root/reference")
+REFERENCE = os.environ.get("LEANSELECT_REFERENCE")
+if not REFERENCE:
+    raise SystemExit("set LEANSELECT_REFERENCE to the LeanSelect source tree")
 sys.path.insert(0, REFERENCE)
 
 from oracle import leanselect_oracle as ora  # noqa: E402
