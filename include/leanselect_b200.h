@@ -132,6 +132,9 @@ int ls_project_queries(const uint16_t* q, int64_t total_q, int32_t num_heads,
  * Page scores [G, total_q, max_pages] fp32, max_pages = ceil(max_seqlen_q/block):
  * row t of sequence b holds the max over atoms [4p-1, 4p+4) of Qs[t]·Ks[a]
  * for p < P_b (no causal mask, as the reference) and -inf for p >= P_b.
+ * Atom scores are rounded to bf16 as the reference's bf16 einsum rounds
+ * them (selector.py:203-207), so every value is a bf16 number; these are
+ * the scores ls_select_pages ranks.
  * q is the post-RoPE query; ks comes from ls_project_atom_keys.  Requires
  * block_size == 64, kernel_stride == 16.
  */
@@ -157,8 +160,8 @@ int ls_atom_scores(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
 
 /*
  * ls_select_pages_workspace_bytes -- bytes of scratch ls_select_pages needs:
- * the pooled page scores of every (group, query row), fp32, rows padded to
- * 8 pages: 4 * G * total_q * round_up(ceil(max_seqlen_q / 64), 8).
+ * the pooled page scores of every (group, query row), bf16, rows padded to
+ * 8 pages: 2 * G * total_q * round_up(ceil(max_seqlen_q / 64), 8).
  */
 size_t ls_select_pages_workspace_bytes(int64_t total_q, int32_t num_kv_heads,
                                        int32_t max_seqlen_q);
@@ -170,7 +173,8 @@ size_t ls_select_pages_workspace_bytes(int64_t total_q, int32_t num_kv_heads,
  *
  * Two kernels: a tcgen05 kernel computes the Q projection, the atom scores
  * and the page max-pool for every (group, row, candidate page) into
- * `workspace`; a warp-per-row radix select then picks the pages.
+ * `workspace` as bf16 (the rounding of the reference's bf16 einsum,
+ * selector.py:203-207); a warp-per-row radix select then picks the pages.
  *
  * topk_idx [G, total_q, take] int32, take = min(topk, max_pages) as in the
  * reference (minicpm.py:3096-3104).  Row t of sequence b holds
@@ -198,9 +202,11 @@ int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
  * minus the workspace: scratch comes from a 16 MiB buffer compiled into the
  * library (one per GPU, held until the process exits), so requests with
  * ls_select_pages_workspace_bytes(total_q, G, max_seqlen_q) above 16 MiB
- * (e.g. one 2-group sequence longer than about 11K tokens) return
- * LS_ERR_UNSUPPORTED.  The first call on each device looks up the buffer's
- * device address; make that first call before any stream capture.  Calls
+ * (e.g. one 2-group sequence longer than 16384 tokens) return
+ * LS_ERR_UNSUPPORTED, after the same argument checks as ls_select_pages.
+ * Each call looks up the buffer's device address on the current device;
+ * the first lookup on a device loads the library's device code there, so
+ * make the first call on each device before any stream capture.  Calls
  * share the buffer: calls that overlap on the GPU race, so serialise them.
  */
 int ls_select_pages_noalloc(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,

@@ -299,16 +299,19 @@ int ls_atom_scores(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
 size_t ls_select_pages_workspace_bytes(int64_t total_q, int32_t num_kv_heads,
                                        int32_t max_seqlen_q) {
   if (total_q <= 0 || num_kv_heads <= 0 || max_seqlen_q <= 0) return 0;
-  return sizeof(float) * select_workspace_floats(total_q * num_kv_heads, (max_seqlen_q + 63) / 64);
+  return select_workspace_bytes(total_q * num_kv_heads, (max_seqlen_q + 63) / 64);
 }
 
-int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
-                    const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_c, int32_t batch,
-                    int32_t max_seqlen_q, int64_t total_q, int64_t total_c, int32_t num_heads,
-                    int32_t num_kv_heads, int32_t head_dim, int32_t width, int32_t take,
-                    int32_t init_blocks, int32_t local_blocks, int32_t block_size,
-                    int32_t kernel_stride, int32_t* topk_idx, void* workspace,
-                    size_t workspace_bytes, int32_t* status, void* stream) {
+}  // extern "C"
+
+namespace ls {
+
+int check_select_args(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                      const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_c, int32_t batch,
+                      int32_t max_seqlen_q, int64_t total_q, int64_t total_c, int32_t num_heads,
+                      int32_t num_kv_heads, int32_t head_dim, int32_t width, int32_t take,
+                      int32_t init_blocks, int32_t local_blocks, int32_t block_size,
+                      int32_t kernel_stride, const int32_t* topk_idx) {
   int rc = check_score_common(q, wq_t, total_q, num_heads, num_kv_heads, head_dim, width);
   if (rc != LS_OK) return rc;
   LS_REQUIRE(cu_seqlens_q && cu_seqlens_c, "null cu_seqlens");
@@ -323,6 +326,25 @@ int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
   LS_REQUIRE(topk_idx, "null topk_idx");
   LS_REQUIRE(total_c == 0 || ks, "null ks");
   if (ks) LS_REQUIRE_ALIGNED(ks);
+  return LS_OK;
+}
+
+}  // namespace ls
+
+extern "C" {
+
+int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                    const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_c, int32_t batch,
+                    int32_t max_seqlen_q, int64_t total_q, int64_t total_c, int32_t num_heads,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t width, int32_t take,
+                    int32_t init_blocks, int32_t local_blocks, int32_t block_size,
+                    int32_t kernel_stride, int32_t* topk_idx, void* workspace,
+                    size_t workspace_bytes, int32_t* status, void* stream) {
+  int rc = check_select_args(q, wq_t, ks, cu_seqlens_q, cu_seqlens_c, batch, max_seqlen_q,
+                             total_q, total_c, num_heads, num_kv_heads, head_dim, width, take,
+                             init_blocks, local_blocks, block_size, kernel_stride, topk_idx);
+  if (rc != LS_OK) return rc;
+  if (total_q == 0 || take == 0) return LS_OK;
   const size_t need = ls_select_pages_workspace_bytes(total_q, num_kv_heads, max_seqlen_q);
   LS_REQUIRE(workspace && workspace_bytes >= need, "workspace too small: %zu < %zu bytes",
              workspace_bytes, need);
@@ -330,7 +352,7 @@ int ls_select_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
   ScoreArgs a{};
   rc = build_score_args(&a, q, wq_t, ks, total_q, total_c, num_heads, num_kv_heads);
   if (rc != LS_OK) return rc;
-  a.workspace = static_cast<float*>(workspace);
+  a.workspace = static_cast<uint16_t*>(workspace);
   a.cu_q = cu_seqlens_q;
   a.cu_c = cu_seqlens_c;
   a.batch = batch;
@@ -405,7 +427,7 @@ int ls_uniform_select_pages(const uint16_t* q, const uint16_t* kc, const int32_t
   ScoreArgs a{};
   int rc = build_score_args(&a, q, wq_t, ks, total_q, total_c, num_heads, num_kv_heads);
   if (rc != LS_OK) return rc;
-  a.workspace = reinterpret_cast<float*>(base);
+  a.workspace = reinterpret_cast<uint16_t*>(base);
   a.cu_q = cu_seqlens_q;
   a.cu_c = cu_seqlens_c;
   a.batch = batch;
@@ -461,7 +483,7 @@ int ls_select_pages_chunk(const uint16_t* q, const uint16_t* wq_t, const uint16_
   a.pos_offset = q_position;
   a.seq_len = seq_len;
   a.topk_idx = topk_idx;
-  a.workspace = static_cast<float*>(workspace);
+  a.workspace = static_cast<uint16_t*>(workspace);
   a.status = status;
   const cudaError_t err = launch_score(kModeSelect, a, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? LS_OK : cuda_fail(err, "select_pages_chunk launch");

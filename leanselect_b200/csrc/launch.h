@@ -47,7 +47,7 @@ struct ScoreArgs {
   int pos_offset;      // chunk mode: position of query row 0 inside its sequence
   int seq_len;         // chunk mode: length of the whole sequence (0 = rows are the sequence)
   int32_t* topk_idx;   // kModeSelect
-  float* workspace;    // kModeSelect: pooled page scores [G, total_q, round8(max_pages)]
+  uint16_t* workspace; // kModeSelect: pooled page scores [G, total_q, round8(max_pages)] bf16
   uint16_t* atom_out;  // kModeAtoms: raw atom scores [G, total_q, max_atoms] bf16
   int max_atoms;       // kModeAtoms: row length of atom_out
   float* page_scores;  // kModeScore
@@ -69,8 +69,9 @@ cudaError_t launch_score(int mode, const ScoreArgs& args, cudaStream_t stream);
 cudaError_t launch_uniform_prep(const uint16_t* kc, int64_t total_c, int num_kv_heads, int hg,
                                 uint16_t* wq_t, uint16_t* ks, cudaStream_t stream);
 
-// Floats of selection workspace for `rows` = G * query rows and `max_pages`.
-size_t select_workspace_floats(int64_t rows, int max_pages);
+// Bytes of selection workspace for `rows` = G * query rows and `max_pages`:
+// one bf16 page score per (row, page), rows padded to 8 pages (16 bytes).
+size_t select_workspace_bytes(int64_t rows, int max_pages);
 
 // Sparse attention (sparse_attn.cu).
 struct AttnArgs {
@@ -102,6 +103,15 @@ cudaError_t launch_sparse_attn(const AttnArgs& args, cudaStream_t stream);
 // nothing is written.  Its duration is the L2 -> shared-memory gather time
 // the attention kernel cannot beat (a measured roofline for it).
 cudaError_t launch_sparse_attn_gather_only(const AttnArgs& args, cudaStream_t stream);
+
+// Host-side argument checks of ls_select_pages other than its workspace
+// (shared with ls_select_pages_noalloc); LS_OK or the LS_ERR_* code it sets.
+int check_select_args(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                      const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_c, int32_t batch,
+                      int32_t max_seqlen_q, int64_t total_q, int64_t total_c, int32_t num_heads,
+                      int32_t num_kv_heads, int32_t head_dim, int32_t width, int32_t take,
+                      int32_t init_blocks, int32_t local_blocks, int32_t block_size,
+                      int32_t kernel_stride, const int32_t* topk_idx);
 
 // Records `message` as the calling thread's ls_last_error() text; returns `code`.
 int set_host_error(int code, const char* message);

@@ -11,10 +11,13 @@
 //
 // The buffer is a file-scope __device__ array of kScratchBytes (16 MiB).
 // Every GPU that loads the library holds its own copy until the process
-// exits.  A host pointer to the array's name is not a device address, so the
-// device address is looked up with cudaGetSymbolAddress, once per device,
-// with that device current, on the first call made on it; make that first
-// call before any stream capture.
+// exits.  A host pointer to the array's name is not a device address, so
+// every call looks the device address up with cudaGetSymbolAddress on the
+// current device.  The first such lookup on a device loads the library's
+// device code there, so make the first call on each device before any
+// stream capture; later lookups are host-side, and looking the address up
+// on every call (rather than caching it) keeps it valid across a
+// cudaDeviceReset.
 //
 // All calls on a device share the one buffer and it keeps the last call's
 // contents.  Nothing in it has to start at zero: the scoring kernel writes
@@ -23,7 +26,6 @@
 // different host threads without ordering) would overwrite each other's
 // scores: serialise them.
 #include <cstdio>
-#include <mutex>
 
 #include "common.cuh"
 #include "launch.h"
@@ -32,28 +34,15 @@ namespace ls {
 namespace {
 
 constexpr size_t kScratchBytes = size_t{16} << 20;
-constexpr int kMaxDevices = 64;
 
-static __device__ __align__(256) float g_select_scratch[kScratchBytes / sizeof(float)];
+static __device__ __align__(256) uint16_t g_select_scratch[kScratchBytes / sizeof(uint16_t)];
 
-std::mutex g_scratch_mutex;
-void* g_scratch_address[kMaxDevices] = {};
-
-// Device address of this device's scratch array (looked up on first use).
+// Device address of the current device's scratch array.
 int scratch_address(void** out) {
-  int dev = -1;
-  cudaError_t err = cudaGetDevice(&dev);
+  void* p = nullptr;
+  const cudaError_t err = cudaGetSymbolAddress(&p, g_select_scratch);
   if (err != cudaSuccess) return set_host_error(LS_ERR_CUDA, cudaGetErrorString(err));
-  if (dev < 0 || dev >= kMaxDevices)
-    return set_host_error(LS_ERR_UNSUPPORTED, "device ordinal beyond the scratch table");
-  std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_address[dev] == nullptr) {
-    void* p = nullptr;
-    err = cudaGetSymbolAddress(&p, g_select_scratch);
-    if (err != cudaSuccess) return set_host_error(LS_ERR_CUDA, cudaGetErrorString(err));
-    g_scratch_address[dev] = p;
-  }
-  *out = g_scratch_address[dev];
+  *out = p;
   return LS_OK;
 }
 
@@ -66,6 +55,12 @@ extern "C" int ls_select_pages_noalloc(
     int64_t total_c, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t width,
     int32_t take, int32_t init_blocks, int32_t local_blocks, int32_t block_size,
     int32_t kernel_stride, int32_t* topk_idx, int32_t* status, void* stream) {
+  // The same argument checks as ls_select_pages first, so a malformed call
+  // gets the same error code; then the built-in buffer's size limit.
+  int rc = ls::check_select_args(q, wq_t, ks, cu_seqlens_q, cu_seqlens_c, batch, max_seqlen_q,
+                                 total_q, total_c, num_heads, num_kv_heads, head_dim, width, take,
+                                 init_blocks, local_blocks, block_size, kernel_stride, topk_idx);
+  if (rc != LS_OK) return rc;
   const size_t need = ls_select_pages_workspace_bytes(total_q, num_kv_heads, max_seqlen_q);
   if (need > ls::kScratchBytes) {
     char msg[256];
@@ -75,8 +70,9 @@ extern "C" int ls_select_pages_noalloc(
              need, ls::kScratchBytes);
     return ls::set_host_error(LS_ERR_UNSUPPORTED, msg);
   }
+  if (total_q == 0 || take == 0) return LS_OK;
   void* scratch = nullptr;
-  const int rc = ls::scratch_address(&scratch);
+  rc = ls::scratch_address(&scratch);
   if (rc != LS_OK) return rc;
   return ls_select_pages(q, wq_t, ks, cu_seqlens_q, cu_seqlens_c, batch, max_seqlen_q, total_q,
                          total_c, num_heads, num_kv_heads, head_dim, width, take, init_blocks,

@@ -329,8 +329,16 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
       fence_proxy_async_smem();
       mbar_arrive(&bars->qs_ready);
 
-      float* out_row = (MODE == kModeScore ? args.page_scores : args.workspace) +
-                       (static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_pages;
+      // Score mode: fp32 page scores of the caller.  Select mode: bf16 page
+      // scores in the workspace (rows padded to a multiple of 8 pages).
+      float* out_row = MODE == kModeScore
+                           ? args.page_scores +
+                                 (static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_pages
+                           : nullptr;
+      uint16_t* ws_row = MODE == kModeSelect
+                             ? args.workspace +
+                                   (static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_pages
+                             : nullptr;
       uint16_t* atom_row = MODE == kModeAtoms
                                ? args.atom_out +
                                      (static_cast<int64_t>(ti.g) * args.total_q + q_row) * args.max_atoms
@@ -378,6 +386,11 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
               }
             }
           } else {
+            // Page p of this block pools atoms [4p-1, 4p+4): its first atom is
+            // the previous block's last one (carry).  The reference rounds the
+            // atom scores to bf16 (its bf16 einsum output, selector.py:203-207)
+            // before pooling; rounding is monotone, so rounding the pooled
+            // maximum once gives the same value.
             float pg[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -385,46 +398,60 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
               pg[i] = fmaxf(m, fmaxf(fmaxf(v[4 * i], v[4 * i + 1]), fmaxf(v[4 * i + 2], v[4 * i + 3])));
             }
             carry = v[31];
-            if (MODE == kModeSelect && args.uniform) {
-#pragma unroll
-              for (int i = 0; i < 8; ++i) pg[i] = uniform_score(pg[i], args.score_scale);
-            }
             const int p0 = j * 32 + q * 8;
-            if (valid && p0 < args.max_pages) {
-              if (MODE == kModeScore) {
+            if constexpr (MODE == kModeSelect) {
+              // Uniform method: bf16(bf16(s) * scale) is already a bf16 value.
+              if (args.uniform) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) pg[i] = uniform_score(pg[i], args.score_scale);
+              }
+              if (valid && p0 < args.max_pages) {
+                uint4 u;
+                u.x = pack_bf16x2(pg[0], pg[1]);
+                u.y = pack_bf16x2(pg[2], pg[3]);
+                u.z = pack_bf16x2(pg[4], pg[5]);
+                u.w = pack_bf16x2(pg[6], pg[7]);
+                *reinterpret_cast<uint4*>(ws_row + p0) = u;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) pg[i] = __bfloat162float(__float2bfloat16_rn(pg[i]));
+              if (valid && p0 < args.max_pages) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
                   if (p0 + i >= ti.pages) pg[i] = -INFINITY;
               }
               if ((args.max_pages & 7) == 0) {
-                // Rows padded to 8 pages (the select workspace): stage the warp's
-                // 32 x 8 block in shared memory and write it back as 32-byte row
-                // segments, two lanes per row.
-                float* st = store_stage + quad * 256;
-                *reinterpret_cast<float4*>(st + lane * 8) = make_float4(pg[0], pg[1], pg[2], pg[3]);
-                *reinterpret_cast<float4*>(st + lane * 8 + 4) = make_float4(pg[4], pg[5], pg[6], pg[7]);
-              } else {
+                // Rows of a multiple of 8 pages: stage the warp's 32 x 8 block
+                // in shared memory and write it back as 32-byte row segments,
+                // two lanes per row.
+                if (valid && p0 < args.max_pages) {
+                  float* st = store_stage + quad * 256;
+                  *reinterpret_cast<float4*>(st + lane * 8) = make_float4(pg[0], pg[1], pg[2], pg[3]);
+                  *reinterpret_cast<float4*>(st + lane * 8 + 4) = make_float4(pg[4], pg[5], pg[6], pg[7]);
+                }
+                if (p0 < args.max_pages) {
+                  __syncwarp();
+                  const float* st = store_stage + quad * 256;
+                  float* wbase = args.page_scores +
+                                 (static_cast<int64_t>(ti.g) * args.total_q + ti.q0 + ti.row0 +
+                                  quad * 32) * args.max_pages + p0;
+#pragma unroll
+                  for (int i = 0; i < 2; ++i) {
+                    const int c = lane + 32 * i;  // row c / 2, half c % 2
+                    const int r = c >> 1;
+                    if (quad * 32 + r < ti.rows)
+                      *reinterpret_cast<float4*>(wbase + static_cast<int64_t>(r) * args.max_pages +
+                                                 4 * (c & 1)) =
+                          *reinterpret_cast<const float4*>(st + r * 8 + 4 * (c & 1));
+                  }
+                  __syncwarp();
+                }
+              } else if (valid && p0 < args.max_pages) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
                   if (p0 + i < args.max_pages) out_row[p0 + i] = pg[i];
               }
-            }
-            if (p0 < args.max_pages && (args.max_pages & 7) == 0) {
-              __syncwarp();
-              const float* st = store_stage + quad * 256;
-              float* wbase = (MODE == kModeScore ? args.page_scores : args.workspace) +
-                             (static_cast<int64_t>(ti.g) * args.total_q + ti.q0 + ti.row0 +
-                              quad * 32) * args.max_pages + p0;
-#pragma unroll
-              for (int i = 0; i < 2; ++i) {
-                const int c = lane + 32 * i;  // row c / 2, half c % 2
-                const int r = c >> 1;
-                if (quad * 32 + r < ti.rows)
-                  *reinterpret_cast<float4*>(wbase + static_cast<int64_t>(r) * args.max_pages +
-                                             4 * (c & 1)) =
-                      *reinterpret_cast<const float4*>(st + r * 8 + 4 * (c & 1));
-              }
-              __syncwarp();
             }
           }
         }
@@ -434,24 +461,29 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
       if (MODE == kModeAtoms && valid && ok) {
         for (int a = ti.atom_tiles * 128; a < args.max_atoms; ++a) atom_row[a] = 0xFF80u;
       }
-      if (MODE != kModeAtoms && valid && ok) {
+      if (MODE == kModeScore && valid && ok) {
         // Pages past the last computed tile: only page 32*tiles can still see
-        // an atom (the last one, carried).  Score mode fills the whole row;
-        // select mode fills up to the row's last candidate page.
-        const int qp = pos / 64;
-        const int end = MODE == kModeScore ? args.max_pages
-                        : args.uniform     ? min(args.max_pages, qp + 2)
-                                           : min(args.max_pages, qp - args.local_blocks);
-        const float tail = (MODE == kModeSelect && args.uniform)
-                               ? uniform_score(carry, args.score_scale) : carry;
-        for (int p = ti.atom_tiles * 32; p < end; ++p)
+        // an atom (the last one, carried).
+        const float tail = __bfloat162float(__float2bfloat16_rn(carry));
+        for (int p = ti.atom_tiles * 32; p < args.max_pages; ++p)
           out_row[p] = (p == ti.atom_tiles * 32 && p < ti.pages) ? tail : -INFINITY;
-        if (MODE == kModeSelect && args.uniform && qp + 1 < ti.pages && qp + 1 < args.max_pages) {
+      }
+      if (MODE == kModeSelect && valid && ok) {
+        // Candidate pages past the last computed tile (up to the row's last
+        // candidate): only page 32*tiles can still see an atom (the carried one).
+        const int qp = pos / 64;
+        const int end = args.uniform ? min(args.max_pages, qp + 2)
+                                     : min(args.max_pages, qp - args.local_blocks);
+        const float tail = args.uniform ? uniform_score(carry, args.score_scale) : carry;
+        const uint16_t tail_bits = __bfloat16_as_ushort(__float2bfloat16_rn(tail));
+        for (int p = ti.atom_tiles * 32; p < end; ++p)
+          ws_row[p] = (p == ti.atom_tiles * 32 && p < ti.pages) ? tail_bits : uint16_t{0xFF80u};
+        if (args.uniform && qp + 1 < ti.pages && qp + 1 < args.max_pages) {
           // Page qp+1 competes as the candidate after the last regular one:
           // move its score into that slot (the first non-sink local page,
           // whose own score is never read; the same thread wrote both).
           const int slot = max(max(0, qp - args.local_blocks), min(args.init_blocks, qp + 1));
-          out_row[slot] = out_row[qp + 1];
+          ws_row[slot] = ws_row[qp + 1];
         }
       }
     }
@@ -470,35 +502,85 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
 // ---------------------------------------------------------------------------
 
 constexpr int kTopkWarps = 8;
-constexpr int kBufCap = 256;         // per-warp candidate buffer (8 blocks of 8 warps fit an SM)
+constexpr int kRowCap = 2048;              // candidates a warp stages in shared memory
+constexpr int kRowChunks = kRowCap / 8 + 1;  // 16-byte chunks, +1 for a misaligned start
+constexpr int kKeptCap = 256;              // candidates kept above the estimated cut
 
-// Order-preserving map of fp32 to uint32; -inf and NaN map to 0 (never picked).
-__device__ __forceinline__ uint32_t score_key(float s) {
-  if (!(s > -INFINITY)) return 0u;  // -inf or NaN
-  const uint32_t u = __float_as_uint(s);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+struct TopkWarpSmem {
+  uint4 row[kRowChunks];        // the row's candidate scores (bf16), 16-byte aligned copy
+  uint32_t hist[256];           // radix / sample histograms
+  uint16_t kept_key[kKeptCap];  // candidates at or above the cut, in candidate order
+  uint16_t kept_idx[kKeptCap];
+};
+
+constexpr size_t topk_smem_bytes() { return kTopkWarps * sizeof(TopkWarpSmem); }
+
+// Order-preserving 16-bit key of a bf16 score; -inf and NaN map to 0 (never
+// picked).  Finite scores map to 0x0080 .. 0xFF7F and +inf to 0xFF80; -0
+// and +0 share a key (they compare equal, so they tie).
+__device__ __forceinline__ uint32_t bf16_key(uint32_t b) {
+  b = b == 0x8000u ? 0u : b;
+  const uint32_t k = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+  return (k <= 0x7Fu || k > 0xFF80u) ? 0u : k;
 }
 
-struct RowKeys {          // candidate i of a workspace row
-  const float* p;
-  __device__ __forceinline__ uint32_t operator()(int i) const { return score_key(p[i]); }
+__device__ __forceinline__ uint32_t chunk_bits(const uint4& v, int e) {
+  const uint32_t w = e < 2 ? v.x : e < 4 ? v.y : e < 6 ? v.z : v.w;
+  return (e & 1) ? (w >> 16) : (w & 0xFFFFu);
+}
+
+// A row's candidates as 16-byte chunks: candidate i is element off + i of
+// the chunk sequence (the copy starts at the 8-page boundary below the first
+// candidate).  Either the warp's shared-memory copy or the workspace row.
+struct SmemChunks {
+  const uint4* p;
+  __device__ __forceinline__ uint4 chunk(int c) const { return p[c]; }
+  __device__ __forceinline__ uint32_t bits(int e) const {
+    return reinterpret_cast<const uint16_t*>(p)[e];
+  }
 };
-struct BufKeys {          // entry j of the warp's filtered buffer
-  const uint32_t* k;
+struct GlobalChunks {
+  const uint4* p;
+  __device__ __forceinline__ uint4 chunk(int c) const { return __ldg(p + c); }
+  __device__ __forceinline__ uint32_t bits(int e) const {
+    return __ldg(reinterpret_cast<const unsigned short*>(p) + e);
+  }
+};
+
+template <class Src>
+struct ChunkKeys {        // key of candidate i
+  Src src;
+  int off;
+  __device__ __forceinline__ uint32_t operator()(int i) const { return bf16_key(src.bits(off + i)); }
+};
+struct KeptKeys {         // entry j of the warp's kept buffer
+  const uint16_t* k;
   __device__ __forceinline__ uint32_t operator()(int j) const { return k[j]; }
 };
 
-// Exact threshold of the `need` largest nonzero keys among keys(0 .. count-1):
-// MSB-first radix select, 4 passes of 8 bits over warp histograms in shared
-// memory.  Returns the threshold key; `need` becomes the number of keys equal
-// to it that belong to the selection (the lowest indices win).
+// Exclusive prefix sum over the warp; returns it and sets `total`.
+__device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  total = __shfl_sync(0xffffffffu, incl, 31);
+  return incl - v;
+}
+
+// Exact threshold of the `need` largest nonzero 16-bit keys among
+// keys(0 .. count-1): MSB-first radix select, 2 passes of 8 bits over a warp
+// histogram in shared memory.  Returns the threshold key; `need` becomes the
+// number of keys equal to it that belong to the selection (lowest indices win).
 template <class Keys>
-__device__ uint32_t radix_threshold(const Keys& keys, int count, int& need, uint32_t* hist,
-                                    int lane) {
+__device__ uint32_t radix_threshold16(const Keys& keys, int count, int& need, uint32_t* hist,
+                                      int lane) {
   uint32_t prefix = 0, mask = 0;
 #pragma unroll 1
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
+  for (int pass = 0; pass < 2; ++pass) {
+    const int shift = 8 - 8 * pass;
     for (int k = lane; k < 256; k += 32) hist[k] = 0;
     __syncwarp();
     for (int i = lane; i < count; i += 32) {
@@ -548,28 +630,22 @@ __device__ uint32_t radix_threshold(const Keys& keys, int count, int& need, uint
   return prefix;
 }
 
-// Writes, in index order, the candidates among keys(0 .. count-1) that are
-// above `thr` plus the first `ties` equal to it (all nonzero keys when
-// `all`), as page numbers `index(j) + base`; candidate `skip` is selected but
-// not written.  Returns the next output position.
+// Writes, in index order, the entries among keys(0 .. count-1) above `thr`
+// plus the first `ties` equal to it, as page numbers `index(j) + base`;
+// candidate `skip` is selected but not written.  Returns the next output
+// position.
 template <class Keys, class Index>
-__device__ int emit_selected(const Keys& keys, const Index& index, int count, bool all,
-                             uint32_t thr, int ties, int skip, int base, int32_t* out, int k_out,
-                             int lane) {
+__device__ int emit_threshold(const Keys& keys, const Index& index, int count, uint32_t thr,
+                              int ties, int skip, int base, int32_t* out, int k_out, int lane) {
   int ties_seen = 0;
   for (int b0 = 0; b0 < count; b0 += 32) {
     const int j = b0 + lane;
     const uint32_t key = j < count ? keys(j) : 0u;
-    bool take;
-    if (all) {
-      take = key != 0u;
-    } else {
-      const bool tie = key == thr && key != 0u;
-      const uint32_t tie_mask = __ballot_sync(0xffffffffu, tie);
-      const int tie_rank = ties_seen + __popc(tie_mask & ((1u << lane) - 1));
-      take = key > thr || (tie && tie_rank < ties);
-      ties_seen += __popc(tie_mask);
-    }
+    const bool tie = key == thr && key != 0u;
+    const uint32_t tie_mask = __ballot_sync(0xffffffffu, tie);
+    const int tie_rank = ties_seen + __popc(tie_mask & ((1u << lane) - 1));
+    ties_seen += __popc(tie_mask);
+    bool take = key > thr || (tie && tie_rank < ties);
     const int i = j < count ? index(j) : -1;
     if (i == skip) take = false;  // the slot page qp+1 won stays empty
     const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
@@ -582,44 +658,190 @@ __device__ int emit_selected(const Keys& keys, const Index& index, int count, bo
 struct Identity {
   __device__ __forceinline__ int operator()(int j) const { return j; }
 };
-struct BufIndex {
-  const int32_t* idx;
+struct KeptIndex {
+  const uint16_t* idx;
   __device__ __forceinline__ int operator()(int j) const { return idx[j]; }
 };
 
-// Exclusive prefix sum over the warp; returns it and sets `total`.
-__device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
-  int incl = v;
+// One pass over candidates 0 .. m-1 in rounds of 32 chunks (lane l takes
+// chunk base + l, eight candidates); candidates whose key satisfies `pred`
+// are handed to `emit(pos, key, i)` with consecutive positions in candidate
+// order.  Returns how many were emitted.
+template <class Src, class Pred, class Emit>
+__device__ int compact_candidates(const Src& src, int off, int m, const Pred& pred, const Emit& emit,
+                                  int lane) {
+  const int nch = (off + m + 7) >> 3;
+  int total = 0;
+  for (int base = 0; base < nch; base += 32) {
+    const int c = base + lane;
+    const uint4 v = c < nch ? src.chunk(c) : make_uint4(0u, 0u, 0u, 0u);
+    uint32_t keys[8];
+    int mine = 0;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int t = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += t;
+    for (int e = 0; e < 8; ++e) {
+      const int i = 8 * c + e - off;
+      const uint32_t key = bf16_key(chunk_bits(v, e));
+      keys[e] = (i >= 0 && i < m && pred(key, i)) ? key : 0u;
+      mine += keys[e] != 0u ? 1 : 0;
+    }
+    int round_total;
+    int pos = total + warp_excl_scan(mine, lane, round_total);
+    if (mine) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (keys[e] != 0u) emit(pos++, keys[e], 8 * c + e - off);
+    }
+    total += round_total;
   }
-  total = __shfl_sync(0xffffffffu, incl, 31);
-  return incl - v;
+  return total;
 }
 
-constexpr int kUnroll = 4;  // float4 loads in flight per lane
+// Selects the top `cap` of the m candidates of one row (ties to the lower
+// candidate index) and writes their pages (n_init + i) to out[k_out ...] in
+// ascending order.  Returns the next output position.
+//
+// Candidates with keys at or above a cut estimated from a 1/8 sample
+// (every 8th round of chunks; a 128-bin histogram over the sample's key
+// range, aiming at ~1.5x the needed count) go to the warp's kept buffer in
+// one pass; the exact radix select then runs over those.  When the estimate
+// kept too few or too many, the exact radix runs over the whole row.
+template <class Src>
+__device__ int select_row(const Src& src, int off, int m, int cap, int skip, int n_init,
+                          int32_t* out, int k_out, TopkWarpSmem* ws, int lane) {
+  if (cap <= 0 || m <= 0) return k_out;
+  const ChunkKeys<Src> row_keys{src, off};
+  if (cap >= m) {
+    // Every finite candidate is selected.
+    return k_out + compact_candidates(
+                       src, off, m, [&](uint32_t key, int i) { return key != 0u && i != skip; },
+                       [&](int pos, uint32_t, int i) { out[k_out + pos] = n_init + i; }, lane);
+  }
+  // ---- 1/8 sample: key range and count.
+  const int nch = (off + m + 7) >> 3;
+  uint32_t kmin = 0xFFFFu, kmax = 0u;
+  int sampled = 0;
+  for (int base = 0; base < nch; base += 256) {
+    const int c = base + lane;
+    if (c < nch) {
+      const uint4 v = src.chunk(c);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = 8 * c + e - off;
+        if (i >= 0 && i < m) {
+          ++sampled;
+          const uint32_t key = bf16_key(chunk_bits(v, e));
+          if (key != 0u) {
+            kmin = min(kmin, key);
+            kmax = max(kmax, key);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sampled += __shfl_xor_sync(0xffffffffu, sampled, o);
+    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+  }
+  uint32_t cut = 1u;  // keep every finite key unless the sample says better
+  if (kmax > kmin) {
+    const uint32_t range = kmax - kmin;
+    const int shift = range > 127u ? (32 - __clz(range)) - 7 : 0;  // (range >> shift) < 128
+    uint32_t* hist = ws->hist;
+    for (int k = lane; k < 128; k += 32) hist[k] = 0;
+    __syncwarp();
+    for (int base = 0; base < nch; base += 256) {
+      const int c = base + lane;
+      if (c < nch) {
+        const uint4 v = src.chunk(c);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = 8 * c + e - off;
+          const uint32_t key = bf16_key(chunk_bits(v, e));
+          if (i >= 0 && i < m && key != 0u) atomicAdd(&hist[(key - kmin) >> shift], 1u);
+        }
+      }
+    }
+    __syncwarp();
+    const int target = max(1, min(sampled, static_cast<int>(1.5f * cap * sampled / m) + 1));
+    uint32_t c4[4];
+    uint32_t lane_sum = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      c4[j] = hist[127 - 4 * lane - j];
+      lane_sum += c4[j];
+    }
+    uint32_t incl = lane_sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const uint32_t excl = incl - lane_sum;
+    const bool here = excl < static_cast<uint32_t>(target) && incl >= static_cast<uint32_t>(target);
+    const uint32_t owner_mask = __ballot_sync(0xffffffffu, here);
+    int bin = 0;
+    if (here) {
+      uint32_t cum = excl;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        cum += c4[j];
+        if (cum >= static_cast<uint32_t>(target)) {
+          bin = 127 - 4 * lane - j;
+          break;
+        }
+      }
+    }
+    if (owner_mask != 0u) {
+      bin = __shfl_sync(0xffffffffu, bin, __ffs(owner_mask) - 1);
+      cut = max(1u, kmin + (static_cast<uint32_t>(bin) << shift));
+    }
+    __syncwarp();
+  }
+  // ---- one pass: keep the candidates at or above the cut, in candidate order.
+  const int kept = compact_candidates(
+      src, off, m, [&](uint32_t key, int) { return key >= cut; },
+      [&](int pos, uint32_t key, int i) {
+        if (pos < kKeptCap) {
+          ws->kept_key[pos] = static_cast<uint16_t>(key);
+          ws->kept_idx[pos] = static_cast<uint16_t>(i);
+        }
+      },
+      lane);
+  __syncwarp();
+  int need = cap;
+  if (kept >= cap && kept <= kKeptCap) {
+    const KeptKeys kk{ws->kept_key};
+    const uint32_t thr = radix_threshold16(kk, kept, need, ws->hist, lane);
+    return emit_threshold(kk, KeptIndex{ws->kept_idx}, kept, thr, need, skip, n_init, out, k_out,
+                          lane);
+  }
+  // ---- exact radix over the whole row (the estimate kept too few or too many).
+  int finite = 0;
+  for (int i = lane; i < m; i += 32) finite += row_keys(i) != 0u;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) finite += __shfl_xor_sync(0xffffffffu, finite, o);
+  if (finite <= cap) {
+    return k_out + compact_candidates(
+                       src, off, m, [&](uint32_t key, int i) { return key != 0u && i != skip; },
+                       [&](int pos, uint32_t, int i) { out[k_out + pos] = n_init + i; }, lane);
+  }
+  const uint32_t thr = radix_threshold16(row_keys, m, need, ws->hist, lane);
+  return emit_threshold(row_keys, Identity{}, m, thr, need, skip, n_init, out, k_out, lane);
+}
 
-// Top-T' of each (group, query) row, one warp per row.  The row's candidate
-// scores are read with 16-byte loads, kUnroll per lane in flight.  Rows with
-// at most kBufCap candidates are copied once into a per-warp shared-memory
-// buffer (as order-preserving keys) and selected there.  Longer rows first
-// estimate a cut from a 1/8 sample (every 8th group of 128 consecutive
-// candidates; linear histogram between the sample's min and max, aiming at
-// ~1.5x the needed count), keep the candidates at or above it in the buffer
-// in one pass and select exactly among those; when the estimate kept too
-// few or too many, the exact radix runs over the whole row.  The result is
-// the same on every path: the T' largest scores, ties to the lower page.
-__global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_constant__ ScoreArgs args) {
-  __shared__ uint32_t hist_all[kTopkWarps][256];
-  __shared__ uint32_t buf_key_all[kTopkWarps][kBufCap];
-  __shared__ int32_t buf_idx_all[kTopkWarps][kBufCap];
+// Top-T' of each (group, query) row, one warp per row.  A row's candidate
+// scores are bf16 values of the workspace; rows of at most kRowCap
+// candidates are first copied into the warp's shared memory with 16-byte
+// loads (all in flight at once), longer rows are read from the workspace.
+// The result is the same on every path: the T' largest scores, ties to the
+// lower page.
+__global__ void __launch_bounds__(kTopkWarps * 32, 4) topk_kernel(const __grid_constant__ ScoreArgs args) {
+  extern __shared__ __align__(16) uint8_t topk_smem_raw[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  uint32_t* hist = hist_all[warp];
-  uint32_t* buf_key = buf_key_all[warp];
-  int32_t* buf_idx = buf_idx_all[warp];
+  TopkWarpSmem* ws = reinterpret_cast<TopkWarpSmem*>(topk_smem_raw) + warp;
   const int64_t rows_total = static_cast<int64_t>(args.num_groups) * args.total_q;
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * kTopkWarps + warp; r < rows_total;
        r += static_cast<int64_t>(gridDim.x) * kTopkWarps) {
@@ -642,7 +864,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
     const int pos = args.pos_offset + static_cast<int>(q_row - q0);
     const int pages = ((args.seq_len > 0 ? args.seq_len : n) + 63) / 64;
     int32_t* out = args.topk_idx + r * args.take;
-    const float* scores = args.workspace + r * args.max_pages;
+    const uint16_t* scores = args.workspace + r * args.max_pages;
 
     // Row geometry (minicpm.py:3121-3138).
     const int qp = pos / 64;
@@ -674,204 +896,29 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
     // the score kernel in slot n_init + m, the first non-sink local page.
     const int sinks_out = min(n_init, take_b);
     for (int k = lane; k < sinks_out; k += 32) out[k] = k;
-    const RowKeys row_keys{scores + n_init};
     int k_out = sinks_out;
 
     if (cap > 0) {
-      // Candidates occupy row positions [n_init, end); rows are 32-byte aligned.
-      const float4* row4 = reinterpret_cast<const float4*>(scores);
-      const int end = n_init + m_all;
-      const int jb = n_init >> 2, je = (end + 3) >> 2;
-      bool done = false;
-      if (m_all <= kBufCap) {
-        // ---- copy the row's keys to shared memory, select there.
-        int finite = 0;
-        for (int base = jb; base < je; base += 32 * kUnroll) {
-          float4 v[kUnroll];
-#pragma unroll
-          for (int u = 0; u < kUnroll; ++u) {
-            const int j = base + 32 * u + lane;
-            v[u] = j < je ? row4[j] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-          }
-#pragma unroll
-          for (int u = 0; u < kUnroll; ++u) {
-            const int p0 = 4 * (base + 32 * u + lane);
-            const float vals[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = p0 + e - n_init;
-              if (i >= 0 && i < m_all) {
-                const uint32_t key = score_key(vals[e]);
-                buf_key[i] = key;
-                finite += key != 0u;
-              }
-            }
-          }
+      // Chunks start at the 8-page boundary below the first candidate (rows
+      // are 16-byte aligned); candidate i is element off + i.
+      const int off = n_init & 7;
+      const uint4* row4 = reinterpret_cast<const uint4*>(scores) + (n_init >> 3);
+      const int nch = (off + m_all + 7) >> 3;
+      if (nch <= kRowChunks) {
+        // Copy the row into shared memory with asynchronous 16-byte copies
+        // (no registers held, every copy of the lane in flight at once).
+        for (int c = lane; c < nch; c += 32) {
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(ws->row + c)),
+                       "l"(row4 + c)
+                       : "memory");
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) finite += __shfl_xor_sync(0xffffffffu, finite, o);
+        asm volatile("cp.async.wait_all;" ::: "memory");
         __syncwarp();
-        const BufKeys bk{buf_key};
-        const bool all = finite <= cap;
-        int need = cap;
-        const uint32_t thr = all ? 0u : radix_threshold(bk, m_all, need, hist, lane);
-        k_out = emit_selected(bk, Identity{}, m_all, all, thr, need, future, n_init, out, k_out, lane);
-        done = true;
+        k_out = select_row(SmemChunks{ws->row}, off, m_all, cap, future, n_init, out, k_out, ws,
+                           lane);
       } else {
-        // ---- 1/8 sample: min, max and count of the finite sampled scores.
-        float smin = INFINITY, smax = -INFINITY;
-        int fs = 0, ns = 0;                              // finite / all sampled candidates
-        const int nblk = (je - jb + 31) >> 5;            // groups of 32 float4 (128 scores)
-        const int sampled_blocks = (nblk + 7) >> 3;
-        for (int sb = 0; sb < sampled_blocks; ++sb) {
-          const int j = jb + 256 * sb + lane;
-          if (j < je) {
-            const float4 v = row4[j];
-            const float vals[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = 4 * j + e - n_init;
-              ns += (i >= 0 && i < m_all) ? 1 : 0;
-              if (i >= 0 && i < m_all && vals[e] > -INFINITY) {
-                ++fs;
-                smin = fminf(smin, vals[e]);
-                smax = fmaxf(smax, vals[e]);
-              }
-            }
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          fs += __shfl_xor_sync(0xffffffffu, fs, o);
-          ns += __shfl_xor_sync(0xffffffffu, ns, o);
-          smin = fminf(smin, __shfl_xor_sync(0xffffffffu, smin, o));
-          smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
-        }
-        uint32_t cut = 1u;  // keep every finite key unless the sample says better
-        if (fs > 0 && smax > smin) {
-          // Linear 128-bin histogram of the sample; the cut is the lower edge of
-          // the bin where the count from the top reaches ~1.5 cap * fs / m_all.
-          const float scale = 128.f / (smax - smin);
-          for (int k = lane; k < 128; k += 32) hist[k] = 0;
-          __syncwarp();
-          for (int sb = 0; sb < sampled_blocks; ++sb) {
-            const int j = jb + 256 * sb + lane;
-            if (j < je) {
-              const float4 v = row4[j];
-              const float vals[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int i = 4 * j + e - n_init;
-                if (i >= 0 && i < m_all && vals[e] > -INFINITY)
-                  atomicAdd(&hist[min(127, static_cast<int>((vals[e] - smin) * scale))], 1u);
-              }
-            }
-          }
-          __syncwarp();
-          const int target = max(1, min(fs, static_cast<int>(1.5f * cap * ns / m_all) + 1));
-          uint32_t c4[4];
-          uint32_t lane_sum = 0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            c4[j] = hist[127 - 4 * lane - j];
-            lane_sum += c4[j];
-          }
-          uint32_t incl = lane_sum;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += t;
-          }
-          const uint32_t excl = incl - lane_sum;
-          const bool here = excl < static_cast<uint32_t>(target) && incl >= static_cast<uint32_t>(target);
-          const uint32_t owner_mask = __ballot_sync(0xffffffffu, here);
-          int bin = 0;
-          if (here) {
-            uint32_t cum = excl;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              cum += c4[j];
-              if (cum >= static_cast<uint32_t>(target)) {
-                bin = 127 - 4 * lane - j;
-                break;
-              }
-            }
-          }
-          if (owner_mask != 0u) {
-            bin = __shfl_sync(0xffffffffu, bin, __ffs(owner_mask) - 1);
-            cut = max(1u, score_key(smin + static_cast<float>(bin) / scale));
-          }
-          __syncwarp();
-        }
-        // ---- one pass: count finite candidates, keep those at or above the cut
-        // (in candidate order).
-        int kept = 0, finite = 0;
-        bool overflow = false;
-        for (int base = jb; base < je; base += 32 * kUnroll) {
-          float4 v[kUnroll];
-#pragma unroll
-          for (int u = 0; u < kUnroll; ++u) {
-            const int j = base + 32 * u + lane;
-            v[u] = j < je ? row4[j] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-          }
-#pragma unroll
-          for (int u = 0; u < kUnroll; ++u) {
-            const int p0 = 4 * (base + 32 * u + lane);
-            const float vals[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-            uint32_t keys[4];
-            int mine = 0;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = p0 + e - n_init;
-              keys[e] = (i >= 0 && i < m_all) ? score_key(vals[e]) : 0u;
-              finite += keys[e] != 0u;
-              mine += (keys[e] >= cut && keys[e] != 0u) ? 1 : 0;
-            }
-            int total;
-            const int at = kept + warp_excl_scan(mine, lane, total);
-            if (!overflow && kept + total > kBufCap) overflow = true;
-            if (!overflow) {
-              int w = at;
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                if (keys[e] >= cut && keys[e] != 0u) {
-                  buf_key[w] = keys[e];
-                  buf_idx[w] = p0 + e - n_init;
-                  ++w;
-                }
-              }
-              kept += total;
-            }
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) finite += __shfl_xor_sync(0xffffffffu, finite, o);
-        __syncwarp();
-        if (finite <= cap) {
-          k_out = emit_selected(row_keys, Identity{}, m_all, true, 0u, 0, future, n_init, out, k_out,
-                                lane);
-          done = true;
-        } else if (!overflow && kept >= cap) {
-          const BufKeys bk{buf_key};
-          int need = cap;
-          const uint32_t thr = radix_threshold(bk, kept, need, hist, lane);
-          k_out = emit_selected(bk, BufIndex{buf_idx}, kept, false, thr, need, future, n_init, out,
-                                k_out, lane);
-          done = true;
-        }
-        __syncwarp();
-      }
-      if (!done) {
-        // ---- exact radix over the whole row.
-        int finite = 0;
-        for (int i = lane; i < m_all; i += 32) finite += row_keys(i) != 0u;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) finite += __shfl_xor_sync(0xffffffffu, finite, o);
-        const bool all = finite <= cap;
-        int need = cap;
-        const uint32_t thr = all ? 0u : radix_threshold(row_keys, m_all, need, hist, lane);
-        k_out = emit_selected(row_keys, Identity{}, m_all, all, thr, need, future, n_init, out, k_out,
-                              lane);
+        k_out = select_row(GlobalChunks{row4}, off, m_all, cap, future, n_init, out, k_out, ws,
+                           lane);
       }
       __syncwarp();
     }
@@ -885,8 +932,8 @@ __global__ void __launch_bounds__(kTopkWarps * 32) topk_kernel(const __grid_cons
 
 }  // namespace
 
-size_t select_workspace_floats(int64_t rows, int max_pages) {
-  return static_cast<size_t>(rows) * static_cast<size_t>((max_pages + 7) & ~7);
+size_t select_workspace_bytes(int64_t rows, int max_pages) {
+  return sizeof(uint16_t) * static_cast<size_t>(rows) * static_cast<size_t>((max_pages + 7) & ~7);
 }
 
 cudaError_t launch_score(int mode, const ScoreArgs& args_in, cudaStream_t stream) {
@@ -926,7 +973,10 @@ cudaError_t launch_score(int mode, const ScoreArgs& args_in, cudaStream_t stream
       if (err != cudaSuccess) return err;
       const int64_t rows = static_cast<int64_t>(args.num_groups) * args.total_q;
       const int64_t blocks = std::min<int64_t>((rows + kTopkWarps - 1) / kTopkWarps, 148 * 16);
-      topk_kernel<<<static_cast<unsigned>(blocks), kTopkWarps * 32, 0, stream>>>(args);
+      err = cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(topk_smem_bytes()));
+      if (err != cudaSuccess) return err;
+      topk_kernel<<<static_cast<unsigned>(blocks), kTopkWarps * 32, topk_smem_bytes(), stream>>>(args);
       break;
     }
     default:

@@ -246,7 +246,12 @@ def project_queries(q: torch.Tensor, wq_t: torch.Tensor, num_kv_heads: int) -> t
 def score_pages(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
                 cu_seqlens_q: torch.Tensor, cu_seqlens_c: torch.Tensor, max_seqlen_q: int,
                 *, block_size: int = 64, kernel_stride: int = 16) -> torch.Tensor:
-    """Pooled page scores ``[G, total_q, ceil(max_seqlen_q/64)]`` fp32 (no causal mask)."""
+    """Pooled page scores ``[G, total_q, ceil(max_seqlen_q/64)]`` (no causal mask).
+
+    Stored as fp32; every value is a bf16 number, because the atom scores are
+    rounded to bf16 as the reference's bf16 einsum rounds them
+    (selector.py:203-207).  These are the scores :func:`select_pages` ranks.
+    """
     dev = _require_cuda(q, ks, cu_seqlens_q, cu_seqlens_c)
     qb = _bf16(q)
     total_q = qb.shape[0]

@@ -9,9 +9,9 @@ methods run the CUDA library on CUDA tensors and raise on CPU tensors.
 
 Numerics: the kernels compute in bf16 with fp32 accumulation.  For bf16
 inputs this is the reference's own rounding (its ``fused_weights`` casts to
-the query dtype and its bf16 ``einsum`` returns bf16).  fp32 inputs are
-rounded to bf16 at the boundary and the results are returned in the input
-dtype.
+the query dtype and its bf16 ``einsum`` calls return bf16: projections and
+atom scores alike).  fp32 inputs are rounded to bf16 at the boundary and
+the results are returned in the input dtype.
 """
 from __future__ import annotations
 

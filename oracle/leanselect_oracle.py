@@ -18,12 +18,14 @@ Numeric policies
 ``policy="bf16"``
     The rounding points of the reference's bf16 model path:
     ``CompressK`` returns bf16 (minicpm.py:1183-1184), ``fused_weights`` casts
-    the fp32 products to the query dtype (selector.py:155-157), and the bf16
+    the fp32 products to the query dtype (selector.py:155-157), the bf16
     ``einsum`` calls of ``project_queries``/``project_atom_keys``
-    (selector.py:177, 188-190) return bf16.  Atom/page scores are kept in
-    fp32 here; the reference rounds them to bf16 (selector.py:203-207), and
-    the set comparison tolerates ties at the budget boundary for exactly that
-    reason.
+    (selector.py:177, 188-190) return bf16, and so does the scoring
+    ``einsum`` (selector.py:203-207): atom scores are rounded to bf16 before
+    the max-pool, exactly as the reference rounds them.  Every contraction
+    here is computed exactly (float64) and rounded once; an implementation
+    that accumulates in fp32 in another order can land one bf16 ulp away
+    when the exact value sits next to a rounding midpoint.
 
 Parity pins
 -----------
@@ -249,10 +251,14 @@ def project_atom_keys(kc: np.ndarray, kv_fused: np.ndarray,
     return _maybe_round(out, policy)
 
 
-def atom_scores(qs: np.ndarray, ks: np.ndarray) -> np.ndarray:
-    """``einsum("gnf,gaf->gna")`` of ``score_pages`` (selector.py:203-207), fp32."""
-    return np.einsum("gnf,gaf->gna", qs.astype(np.float64), ks.astype(np.float64),
-                     optimize=True).astype(np.float32)
+def atom_scores(qs: np.ndarray, ks: np.ndarray, policy: str = "fp32") -> np.ndarray:
+    """``einsum("gnf,gaf->gna")`` of ``score_pages`` (selector.py:203-207).
+
+    The einsum returns the operands' dtype: bf16 scores under the bf16 policy.
+    """
+    out = np.einsum("gnf,gaf->gna", qs.astype(np.float64), ks.astype(np.float64),
+                    optimize=True).astype(np.float32)
+    return _maybe_round(out, policy)
 
 
 # ----------------------------------------------------------------------------
@@ -290,7 +296,7 @@ def score_pages(q: np.ndarray, kc: np.ndarray, params: SelectorParams, *, seq_le
     q_fused, kv_fused = fold_weights(params, policy)
     qs = project_queries(q, q_fused, params.num_kv_heads, policy)
     ks = project_atom_keys(kc, kv_fused, policy)
-    return pool_atoms_to_pages(atom_scores(qs, ks), seq_len, block_size, kernel_stride)
+    return pool_atoms_to_pages(atom_scores(qs, ks, policy), seq_len, block_size, kernel_stride)
 
 
 # ----------------------------------------------------------------------------
@@ -395,14 +401,24 @@ def lightweight_compressed_attention(q: np.ndarray, kc: np.ndarray, cu_seqlens_q
     return Selection(idx, boundary, scores_out)
 
 
+def bf16_ulp(x: float) -> float:
+    """Spacing of bfloat16 values at ``|x|`` (2**(e - 7) for 2**e <= |x| < 2**(e+1))."""
+    x = abs(float(x))
+    if not np.isfinite(x) or x == 0.0:
+        return 0.0
+    return 2.0 ** (math.floor(math.log2(x)) - 7)
+
+
 def selection_mismatches(actual: np.ndarray, selection: Selection, *, rel_tol: float = 1e-3,
-                         abs_floor: float = 1e-6):
+                         abs_floor: float = 1e-6, ulps: int = 0):
     """Rows whose page set differs from the oracle beyond a boundary tie.
 
     For each row the symmetric difference between ``actual`` and the oracle
     set must consist only of pages whose oracle score lies within
-    ``rel_tol * |boundary|`` (plus ``abs_floor``) of the row's boundary score,
-    and both sets must have the same size.  Returns a list of
+    ``rel_tol * |boundary|`` (plus ``abs_floor``) of the row's boundary score
+    -- or, with ``ulps``, within that many bf16 ulps of it (two bf16-rounded
+    scores computed with different fp32 accumulation orders can differ by
+    one ulp) -- and both sets must have the same size.  Returns a list of
     ``(g, t, missing, extra)`` for the rows that fail.
     """
     expected = selection.topk_idx
@@ -425,7 +441,7 @@ def selection_mismatches(actual: np.ndarray, selection: Selection, *, rel_tol: f
             if not score_rows:
                 score_rows = _score_lookup(selection)
             row = score_rows[(g, t)]
-            tol = rel_tol * abs(bnd) + abs_floor
+            tol = max(rel_tol * abs(bnd) + abs_floor, ulps * bf16_ulp(bnd))
             if all(abs(float(row[p]) - bnd) <= tol for p in (a ^ e)):
                 continue
             bad.append((g, t, sorted(e - a), sorted(a - e)))
@@ -599,11 +615,23 @@ def select_for_queries(q_rows: np.ndarray, positions, seq_len: int, kc: np.ndarr
     long benchmark configurations can be checked (and timed on the CPU) on a
     sample without scoring every row.  ``take`` is the output width.
     """
-    positions = np.asarray(positions, dtype=np.int64)
     q_fused, kv_fused = fold_weights(params, policy)
     qs = project_queries(q_rows, q_fused, params.num_kv_heads, policy)
     ks = project_atom_keys(kc, kv_fused, policy)
-    pages = pool_atoms_to_pages(atom_scores(qs, ks), seq_len, block_size, kernel_stride)
+    pages = pool_atoms_to_pages(atom_scores(qs, ks, policy), seq_len, block_size, kernel_stride)
+    return select_from_scores(pages, positions, take=take, init_blocks=init_blocks,
+                              local_blocks=local_blocks, block_size=block_size)
+
+
+def select_from_scores(pages: np.ndarray, positions, *, take: int, init_blocks: int = 1,
+                       local_blocks: int = 2, block_size: int = 64) -> Selection:
+    """Masking + top-k (minicpm.py:3124-3141) of given pooled page scores.
+
+    ``pages [G, R, P]`` are the unmasked page scores of query rows at
+    ``positions`` (inside one sequence of ``P`` pages); same rules and tie
+    break as :func:`select_pages`.
+    """
+    positions = np.asarray(positions, dtype=np.int64)
     g, r, p = pages.shape
     qpage = positions // block_size
     page_ids = np.arange(p)

@@ -210,7 +210,70 @@ def bf16_selection_case():
     np.savez_compressed(
         HERE / "bf16_selection.npz", seed=np.int64(3),
         input_digest=np.array(digest(inputs.q, inputs.k, inputs.v)),
-        kc=kc_ref.float().numpy(), qs=qs, ks=ks, idx=canon(idx))
+        kc=kc_ref.float().numpy(), qs=qs, ks=ks, idx=canon(idx),
+        page_bits=reference_page_scores(sel, q16, kc_ref, 1024))
+
+
+def reference_page_scores(sel, q, kc, seq_len):
+    """The reference's pooled page scores (``score_pages``, selector.py:192-214), bf16 bits."""
+    with torch.no_grad():
+        pages = sel.score_pages(q, kc, seq_len=seq_len, block_size=64, kernel_stride=16)
+    return pages.contiguous().view(torch.int16).numpy()
+
+
+def stock_budget_cases():
+    """bf16 selection at the reference's stock budget and at the benchmark's.
+
+    The reference's defaults are ``window_size=2048`` -> ``local_blocks=32``
+    and ``topk = 64 + 32 = 96`` (models/__init__.py:119-127,
+    minicpm.py:1957-1966).  Cases: one 8192-token sequence and a ragged pack
+    with sequences shorter than the 33 forced pages, at T=96 / local 32; and
+    one 16384-token sequence at the benchmark budget T=67 / local 2.  A row
+    sample of each ``topk_idx`` is stored, with the reference's own bf16
+    page scores of those rows (to pin scoring and selection separately).
+    """
+    out = {}
+    specs = [
+        # name, lens, topk, init, local, seed
+        ("stock_8k", [8192], 96, 1, 32, 31),
+        ("stock_ragged", [3000, 1500, 64, 20, 2100, 900], 96, 1, 32, 32),
+        ("bench_16k", [16384], 67, 1, 2, 33),
+    ]
+    for name, lens, topk, init, local, seed in specs:
+        inputs = ora.synthetic_layer(lens, seed=seed, bf16=True)
+        q16 = torch.from_numpy(inputs.q).bfloat16()
+        kc_ref, cu_c = CompressK(2, 128, kernel_size=32, kernel_stride=16)(
+            torch.from_numpy(inputs.k).bfloat16(), torch.from_numpy(inputs.cu_seqlens))
+        sel = make_selector(inputs.params)
+        idx = canon(reference_select(sel, q16, kc_ref, inputs.cu_seqlens, cu_c.numpy(), topk=topk,
+                                     init_blocks=init, local_blocks=local))
+        rows, scores = [], []
+        cu, cc = inputs.cu_seqlens, cu_c.numpy()
+        for b, n in enumerate(lens):
+            r = np.unique(np.concatenate([np.arange(0, n, 7), np.arange(max(0, n - 32), n)]))
+            rows.append(r + cu[b])
+            if cc[b + 1] > cc[b]:
+                bits = reference_page_scores(sel, q16[cu[b]:cu[b] + n], kc_ref[cc[b]:cc[b + 1]], n)
+                scores.append(bits[:, r[::4]])
+        rows = np.concatenate(rows).astype(np.int32)
+        out[f"{name}__lens"] = np.array(lens, dtype=np.int64)
+        out[f"{name}__seed"] = np.int64(seed)
+        out[f"{name}__topk"] = np.int64(topk)
+        out[f"{name}__init"] = np.int64(init)
+        out[f"{name}__local"] = np.int64(local)
+        out[f"{name}__input_digest"] = np.array(digest(inputs.q, inputs.k, inputs.v))
+        out[f"{name}__kc"] = kc_ref.view(torch.int16).numpy()
+        out[f"{name}__cu_c"] = cc
+        out[f"{name}__rows"] = rows
+        out[f"{name}__idx_rows"] = idx[:, rows].astype(np.int16)
+        # Page scores of every 4th sampled row of each sequence with atoms,
+        # concatenated along the row axis and padded to the widest row.
+        width = max(s.shape[-1] for s in scores)
+        padded = [np.pad(s, ((0, 0), (0, 0), (0, width - s.shape[-1])), constant_values=-128)
+                  for s in scores]   # -128 = 0xFF80, bf16 -inf
+        out[f"{name}__page_bits"] = np.concatenate(padded, axis=1)
+    out["names"] = np.array([s[0] for s in specs])
+    np.savez_compressed(HERE / "stock_budget.npz", **out)
 
 
 def uniform_cases():
@@ -296,16 +359,24 @@ def selector_init_cases():
         out[f"{i}_seed"] = np.int64(100 + i)
     np.savez_compressed(HERE / "selector_init.npz", **out)
 
+CASES = {
+    "known_answers": known_answers,
+    "compression": compression_cases,
+    "selector": selector_cases,
+    "selection": selection_cases,
+    "config0": config0_case,
+    "bf16_selection": bf16_selection_case,
+    "stock_budget": stock_budget_cases,
+    "uniform": uniform_cases,
+    "nosa": nosa_atom_score_cases,
+    "selector_init": selector_init_cases,
+}
+
 if __name__ == "__main__":
-    torch.manual_seed(0)
-    known_answers()
-    compression_cases()
-    selector_cases()
-    selection_cases()
-    config0_case()
-    bf16_selection_case()
-    uniform_cases()
-    nosa_atom_score_cases()
-    selector_init_cases()
+    # With arguments only the named cases are (re)written.
+    wanted = sys.argv[1:] or list(CASES)
+    for name in wanted:
+        torch.manual_seed(0)
+        CASES[name]()
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)

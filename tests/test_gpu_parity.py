@@ -3,9 +3,16 @@
 Tolerances:
 * compression and weight folding: bit-exact (same fp32 summation order);
 * projections: within one bf16 ulp, >= 99% bit-exact;
-* page scores: |gpu - oracle| <= 2e-3 + 2e-3*|oracle| (fp32 accumulation order);
+* page scores: bf16 values (the reference's bf16 einsum output), within one
+  bf16 ulp + 2e-3 of the oracle's, >= 98% bit-identical, max abs <= 2e-2 and
+  mean abs <= 2e-3 (north_star); the GPU accumulates the same bf16 products
+  in fp32 in another order, which moves a score across a bf16 rounding point
+  now and then;
 * page selection: identical sets per row except pages whose oracle score is
-  within 1e-3 relative of the row's budget-boundary score;
+  within 1e-3 relative of the row's budget-boundary score (with bf16 scores:
+  exact ties) or, for the rare rows where accumulation order moved a
+  boundary score, one bf16 ulp of it (<= 0.5% of rows); given the GPU's own
+  page scores, the top-k is bit-exact;
 * attention output: max abs <= 2e-2, mean abs <= 2e-3 vs the fp32 oracle, and
   the error RMS below 1% of the output RMS.
 """
@@ -143,6 +150,20 @@ def test_project_atom_keys():
 # a5/a6: page scores
 # ---------------------------------------------------------------------------
 
+def _scores_close(got, want):
+    """bf16 page scores: within one bf16 ulp (+2e-3 near cancellation), mostly identical."""
+    fin = np.isfinite(want)
+    assert np.array_equal(fin, np.isfinite(got))
+    assert np.array_equal(got[~fin], want[~fin])
+    g, w = got[fin], want[fin]
+    err = np.abs(g - w)
+    assert np.all(err <= 2 ** -7 * np.abs(w) + 2e-3), err.max()
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())
+    assert np.mean(err == 0) >= 0.98, np.mean(err == 0)
+    # The values are bf16 numbers.
+    assert np.array_equal(g, ora.bf16_round(g))
+
+
 def test_score_pages_single_sequence_api():
     inp = ora.synthetic_layer([1500], num_heads=32, num_kv_heads=2, head_dim=128, router_heads=32,
                               router_dim=4, hot_pages=5, seed=23, bf16=True)
@@ -152,7 +173,7 @@ def test_score_pages_single_sequence_api():
                           kernel_stride=16).float().cpu().numpy()
     want = ora.score_pages(inp.q, kc, inp.params, seq_len=1500, policy="bf16")
     assert got.shape == want.shape == (2, 1500, 24)
-    np.testing.assert_allclose(got, want, rtol=2e-3, atol=2e-3)
+    _scores_close(got, want)
 
 
 def test_score_pages_packed_batch():
@@ -171,7 +192,7 @@ def test_score_pages_packed_batch():
         if c1 > c0:
             want = ora.score_pages(inp.q[q0:q0 + n], kc[c0:c1], inp.params, seq_len=n,
                                    policy="bf16")
-            np.testing.assert_allclose(got[:, q0:q0 + n, :p], want, rtol=2e-3, atol=2e-3)
+            _scores_close(got[:, q0:q0 + n, :p], want)
         else:
             assert np.all(np.isneginf(got[:, q0:q0 + n, :p]))
         assert np.all(np.isneginf(got[:, q0:q0 + n, p:]))
@@ -190,7 +211,21 @@ SELECT_CASES = [
     ([1300], 32, 2, 4, 32, 11, 3, 4),       # several sinks
     ([1000, 2100], 16, 2, 4, 32, 20, 1, 2),  # 8 heads per group
     ([4096], 32, 2, 4, 32, 128, 1, 2),      # the largest budget
+    # The reference's stock budget: window 2048 -> 32 local pages, topk
+    # 64 + 32 = 96 (models/__init__.py:119-127, minicpm.py:1957-1966);
+    # sequences shorter than the 33 forced pages in the pack.
+    ([8192], 32, 2, 4, 32, 96, 1, 32),
+    ([3000, 1500, 64, 20, 2100, 900, 2111], 32, 2, 4, 32, 96, 1, 32),
 ]
+
+
+def _selection_check(got, want, rows=None):
+    """Sets identical up to boundary ties; one-ulp allowance on <= 0.5% of rows."""
+    bad = ora.selection_mismatches(got, want, rel_tol=1e-3, ulps=1)
+    assert not bad, bad[:5]
+    strict = ora.selection_mismatches(got, want, rel_tol=1e-3)
+    n_rows = got.shape[0] * got.shape[1]
+    assert len(strict) <= max(1, 0.005 * n_rows), (len(strict), n_rows, strict[:3])
 
 
 def _run_selection(lens, h, g, rh, rd, topk, init, local, seed):
@@ -214,8 +249,7 @@ def test_select_pages_matches_oracle(case):
                                                 policy="bf16")
     got_np = got.cpu().numpy()
     assert got.dtype == torch.int32 and got_np.shape == want.topk_idx.shape
-    bad = ora.selection_mismatches(got_np, want, rel_tol=1e-3)
-    assert not bad, bad[:5]
+    _selection_check(got_np, want)
     # No duplicates, padding only at the end of each row.
     for row in got_np.reshape(-1, got_np.shape[-1])[::97]:
         valid = row[row >= 0]
@@ -238,8 +272,112 @@ def test_select_config1_rows():
     rows = np.unique(np.concatenate([np.arange(0, 130), np.arange(n - 70, n),
                                      rng.integers(0, n, 200)]))
     want = ora.select_rows(inp.q, kc, inp.params, rows, take=67)
-    bad = ora.selection_mismatches(got[:, rows], want, rel_tol=1e-3)
-    assert not bad, bad[:5]
+    _selection_check(got[:, rows], want)
+
+
+@pytest.mark.parametrize("case", [0, 1, 4, 6, 7, 8])
+def test_topk_exact_on_gpu_page_scores(case):
+    """The top-k stage alone is bit-exact: the oracle's masking and top-k
+    (lowest page wins ties) applied to the GPU's own page scores reproduce
+    the GPU's selection exactly, sinks, locals and padding included."""
+    lens, h, g, rh, rd, topk, init, local = SELECT_CASES[case]
+    inp = ora.synthetic_layer(lens, num_heads=h, num_kv_heads=g, head_dim=128, router_heads=rh,
+                              router_dim=rd, hot_pages=4, seed=140 + case, bf16=True)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    w = selector_for(inp.params).kernel_weights()
+    ks = ops.project_atom_keys(to_dev(kc), w.wk_t)
+    q, cq, cc = to_dev(inp.q), cu_dev(inp.cu_seqlens), cu_dev(cu_c)
+    take = min(topk, max((n + 63) // 64 for n in lens))
+    got = ops.select_pages(q, w, ks, cq, cc, max(lens), take=take, init_blocks=init,
+                           local_blocks=local).cpu().numpy()
+    pages = ops.score_pages(q, w, ks, cq, cc, max(lens)).cpu().numpy()
+    for b, n in enumerate(lens):
+        q0 = int(inp.cu_seqlens[b])
+        if n == 0:
+            continue
+        if cu_c[b + 1] == cu_c[b]:
+            assert np.all(got[:, q0:q0 + n] == -1)
+            continue
+        p = (n + 63) // 64
+        idx, _, _ = ora.select_pages(pages[:, q0:q0 + n, :p], take=take, init_blocks=init,
+                                     local_blocks=local)
+        np.testing.assert_array_equal(got[:, q0:q0 + n], idx)
+    assert ops.check_status(DEV) == 0
+
+
+@pytest.mark.parametrize("name", ["stock_8k", "stock_ragged", "bench_16k"])
+def test_selection_matches_reference_fixture(name):
+    """GPU selection against the reference's own ``topk_idx`` (tests/golden,
+    written by make_golden.py from ``_lightweight_compressed_attention``):
+    the reference's stock budget (T=96, 32 local pages) and the benchmark's
+    (T=67), bf16, on the reference's own compressed keys.  Differences only
+    at the budget boundary: exact ties, or one bf16 ulp on <= 0.5% of rows."""
+    import pathlib
+    g = np.load(pathlib.Path(__file__).parent / "golden" / "stock_budget.npz")
+    lens = g[f"{name}__lens"].tolist()
+    inp = ora.synthetic_layer(lens, seed=int(g[f"{name}__seed"]), bf16=True)
+    topk, init, local = (int(g[f"{name}__{k}"]) for k in ("topk", "init", "local"))
+    kc = ora.from_bf16_bits(g[f"{name}__kc"].view(np.uint16))
+    cu, cu_c = inp.cu_seqlens, g[f"{name}__cu_c"]
+    view_cfg = lsb.LayerConfig(topk=topk, init_blocks=init, local_blocks=local)
+    from leanselect_b200.attention import _LayerView
+    got = lsb.lightweight_compressed_attention(_LayerView(view_cfg, selector_for(inp.params)),
+                                               to_dev(inp.q), to_dev(kc), cu_dev(cu),
+                                               cu_dev(cu_c), max(lens)).cpu().numpy()
+    rows = g[f"{name}__rows"]
+    ref = g[f"{name}__idx_rows"].astype(np.int32)
+    assert got.shape[2] == ref.shape[2]
+    for b, n in enumerate(lens):
+        mine = (rows >= cu[b]) & (rows < cu[b + 1])
+        sel_rows = rows[mine]
+        c0, c1 = int(cu_c[b]), int(cu_c[b + 1])
+        if c1 == c0:
+            assert np.all(got[:, sel_rows] == -1) and np.all(ref[:, mine] == -1)
+            continue
+        scores = ora.select_for_queries(inp.q[sel_rows], sel_rows - cu[b], n, kc[c0:c1],
+                                        inp.params, take=ref.shape[2], init_blocks=init,
+                                        local_blocks=local)
+        ref_sel = ora.Selection(ref[:, mine], scores.boundary, scores.page_scores)
+        _selection_check(got[:, sel_rows], ref_sel)
+    assert ops.check_status(DEV) == 0
+
+
+def test_long_rows_take_the_global_path_exact_ties():
+    """Rows of more than 2048 candidates (past 131072 tokens) are selected
+    from the workspace instead of the per-warp shared-memory copy.  With a
+    zero head mix every score ties, so the answer is known for every row:
+    the sinks, the lowest candidate pages, the local pages."""
+    from leanselect_b200.sweep import config1_layer, make_selector
+
+    n, T = 147456, 67
+    q, _, _ = config1_layer(n, DEV, 6)
+    k = torch.randn(n, 2, 128, device=DEV).bfloat16()
+    sel = make_selector(DEV, 6)
+    with torch.no_grad():
+        sel.head_mix.zero_()
+    w = sel.kernel_weights()
+    cu = torch.tensor([0, n], dtype=torch.int32, device=DEV)
+    kc, cu_c = ops.compress_keys(k, cu, lengths=[n])
+    ks = ops.project_atom_keys(kc, w.wk_t)
+    idx = ops.select_pages(q, w, ks, cu, cu_c, n, take=T)
+    assert ops.check_status(DEV) == 0
+    qp = np.arange(n) // 64
+    lo = np.maximum(0, qp - 2)                    # local pages lo .. qp
+    local0 = np.maximum(lo, 1)                    # ... minus the sink
+    n_local = qp - local0 + 1
+    cap = np.clip(np.minimum(T - 1 - n_local, lo - 1), 0, None)   # candidates 1 .. lo-1
+    cols = np.arange(T)[None, :]
+    want = np.full((n, T), -1, dtype=np.int32)
+    want[:, 0] = 0
+    dyn = (cols >= 1) & (cols <= cap[:, None])
+    want[dyn] = np.broadcast_to(cols, want.shape)[dyn]
+    start = 1 + cap[:, None]
+    loc = (cols >= start) & (cols < start + n_local[:, None])
+    want[loc] = (local0[:, None] + cols - start)[loc]
+    assert int(cap.max()) == T - 4 and int(lo.max() - 1) > 2048   # rows past the buffer exist
+    got = idx.cpu().numpy()
+    for g in range(2):
+        np.testing.assert_array_equal(got[g], want)
 
 
 @pytest.mark.parametrize("method", ["leanselect", "uniform"])
@@ -311,8 +449,7 @@ def test_full_size_selection_properties_and_row_parity():
     q_rows = q[torch.from_numpy(rows).to(DEV)].float().cpu().numpy()
     want = ora.select_for_queries(q_rows, rows, n, kc.float().cpu().numpy(), params, take=T)
     got = idx.cpu().numpy()[:, rows]
-    bad = ora.selection_mismatches(got, want, rel_tol=1e-3)
-    assert not bad, bad[:5]
+    _selection_check(got, want)
 
     out = ops.sparse_attn(q, k, v, cu, cu, n, n, idx)
     assert ops.check_status(DEV) == 0
@@ -533,8 +670,7 @@ def test_per_sequence_budgets_match_oracle():
             topk=config4_budget(n), policy="bf16")
         got = idx[:, q0:q0 + n, :want.topk_idx.shape[2]]
         assert np.all(idx[:, q0:q0 + n, want.topk_idx.shape[2]:] == -1)
-        bad = ora.selection_mismatches(got, want, rel_tol=1e-3)
-        assert not bad, bad[:3]
+        _selection_check(got, want)
     ref, _ = ora.sparse_attention(inp.q, inp.k, inp.v, inp.cu_seqlens, inp.cu_seqlens, idx)
     _attn_check(out, None, ref, None)
 

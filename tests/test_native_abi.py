@@ -65,14 +65,37 @@ def test_unsupported_geometry_is_reported():
 
 def test_workspace_size_and_check():
     lib = _native.load()
-    # 2 groups x 1000 rows x round8(ceil(1000/64) = 16) pages x 4 bytes
-    assert lib.ls_select_pages_workspace_bytes(1000, 2, 1000) == 2 * 1000 * 16 * 4
-    assert lib.ls_select_pages_workspace_bytes(1000, 2, 1100) == 2 * 1000 * 24 * 4
+    # 2 groups x 1000 rows x round8(ceil(1000/64) = 16) pages x 2 bytes (bf16 scores)
+    assert lib.ls_select_pages_workspace_bytes(1000, 2, 1000) == 2 * 1000 * 16 * 2
+    assert lib.ls_select_pages_workspace_bytes(1000, 2, 1100) == 2 * 1000 * 24 * 2
     fake = ctypes.c_void_p(1 << 20)
     rc = lib.ls_select_pages(fake, fake, fake, fake, fake, 1, 1000, 1000, 61, 32, 2, 128, 128, 35,
                              1, 2, 64, 16, fake, fake, 100, None, None)
     assert rc == _native.LS_ERR_INVALID_ARGUMENT
     assert b"workspace" in lib.ls_last_error()
+
+
+def test_noalloc_checks_arguments_before_its_scratch_limit():
+    """A malformed call gets ls_select_pages' own error, not the scratch-size one;
+    a well-formed call one token past the 16 MiB limit gets LS_ERR_UNSUPPORTED."""
+    lib = _native.load()
+    fake = ctypes.c_void_p(1 << 20)
+    # head_dim 64 on a request far beyond the scratch: the geometry error wins.
+    rc = lib.ls_select_pages_noalloc(fake, fake, fake, fake, fake, 1, 65536, 65536, 4095, 32, 2,
+                                     64, 128, 67, 1, 2, 64, 16, fake, None, None)
+    assert rc == _native.LS_ERR_UNSUPPORTED
+    assert b"head_dim" in lib.ls_last_error()
+    rc = lib.ls_select_pages_noalloc(fake, fake, fake, fake, fake, 1, 65536, 65536, 4095, 32, 2,
+                                     128, 128, 67, 1, 2, 64, 16, None, None, None)
+    assert rc == _native.LS_ERR_INVALID_ARGUMENT
+    assert b"topk_idx" in lib.ls_last_error()
+    # 16384 tokens x 2 groups x 256 pages x 2 bytes is exactly 16 MiB; one more token is not.
+    assert lib.ls_select_pages_workspace_bytes(16384, 2, 16384) == 16 << 20
+    assert lib.ls_select_pages_workspace_bytes(16385, 2, 16385) > 16 << 20
+    rc = lib.ls_select_pages_noalloc(fake, fake, fake, fake, fake, 1, 16385, 16385, 1023, 32, 2,
+                                     128, 128, 67, 1, 2, 64, 16, fake, None, None)
+    assert rc == _native.LS_ERR_UNSUPPORTED
+    assert b"scratch" in lib.ls_last_error()
 
 
 def test_misaligned_pointer_is_reported():
@@ -184,7 +207,7 @@ def test_uniform_and_atom_score_entry_points_validate_on_host():
     fake = ctypes.c_void_p(1 << 20)
     # 2 groups x (16 heads x 128 x 128 bf16 weights, padded) + Ks + selection workspace
     need = lib.ls_uniform_select_workspace_bytes(1000, 61, 32, 2, 1000)
-    assert need == 32 * 128 * 128 * 2 + (2 * 61 * 128 * 2 + 255) // 256 * 256 + 2 * 1000 * 16 * 4
+    assert need == 32 * 128 * 128 * 2 + (2 * 61 * 128 * 2 + 255) // 256 * 256 + 2 * 1000 * 16 * 2
     rc = lib.ls_uniform_select_pages(fake, fake, fake, fake, 1, 1000, 1000, 61, 32, 2, 128, 35, 1,
                                      2, 64, 16, 0.0, fake, fake, need - 1, None, None)
     assert rc == _native.LS_ERR_INVALID_ARGUMENT and b"workspace" in lib.ls_last_error()

@@ -161,10 +161,17 @@ def test_bf16_selection_matches_reference():
     np.testing.assert_allclose(ks, g["ks"], rtol=2 ** -7, atol=1e-6)
     sel = ora.lightweight_compressed_attention(inputs.q, g["kc"], inputs.cu_seqlens, cu_c,
                                                inputs.params, topk=19, policy="bf16")
-    # The reference rounds atom scores to bf16 (relative step 2**-8), which
-    # creates exact ties; those are tolerated at the same relative width.
-    bad = ora.selection_mismatches(g["idx"], sel, rel_tol=2 ** -7)
-    assert len(bad) <= 0.01 * sel.topk_idx.shape[0] * sel.topk_idx.shape[1], bad[:5]
+    # Atom scores are rounded to bf16 as the reference rounds them, so the
+    # sets differ only by exact ties at the budget boundary (torch.topk
+    # breaks them its own way), inside north_star's 1e-3 band.
+    bad = ora.selection_mismatches(g["idx"], sel, rel_tol=1e-3)
+    assert not bad, bad[:5]
+    # The reference's own page scores (bf16) against the oracle's.
+    ref_pages = ora.from_bf16_bits(g["page_bits"].view(np.uint16))
+    mine = ora.score_pages(inputs.q, g["kc"], inputs.params, seq_len=1024, policy="bf16")
+    err = np.abs(mine - ref_pages)
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3
+    assert np.mean(err == 0) > 0.98
 
 
 def _sdpa_reference(q, k, v, cu, idx, causal=True):
@@ -339,3 +346,73 @@ def test_nosa_atom_scores_match_reference():
             np.testing.assert_allclose(got, want, rtol=2 ** -7, atol=2e-3)
             assert np.mean(got == want) > 0.95
         assert np.all(np.isneginf(rows[..., c1 - c0:]))
+
+
+STOCK_CASES = ["stock_8k", "stock_ragged", "bench_16k"]
+
+
+def _stock_case(name):
+    g = load("stock_budget.npz")
+    lens = g[f"{name}__lens"].tolist()
+    inputs = ora.synthetic_layer(lens, seed=int(g[f"{name}__seed"]), bf16=True)
+    assert digest(inputs.q, inputs.k, inputs.v) == str(g[f"{name}__input_digest"])
+    kc = ora.from_bf16_bits(g[f"{name}__kc"].view(np.uint16))
+    return g, lens, inputs, kc
+
+
+@pytest.mark.parametrize("name", STOCK_CASES)
+def test_stock_budget_selection_matches_reference(name):
+    """bf16 selection at the reference's stock budget (T=96, 32 local pages,
+    models/__init__.py:119-127) and at the benchmark's (T=67, local 2).
+
+    Three pins: (1) given the reference's own bf16 page scores, the oracle's
+    masking and top-k pick the reference's sets exactly (exact score ties
+    aside); (2) the oracle's page scores equal the reference's except for
+    rare one-ulp differences of fp32 accumulation order; (3) end to end, the
+    oracle's selection differs from the reference's only by exact ties at the
+    budget boundary (north_star's 1e-3 band).
+    """
+    g, lens, inputs, kc = _stock_case(name)
+    topk, init, local = (int(g[f"{name}__{k}"]) for k in ("topk", "init", "local"))
+    cu, cu_c = inputs.cu_seqlens, g[f"{name}__cu_c"]
+    ekc, ecu = ora.compress_keys(inputs.k, cu, policy="bf16")
+    np.testing.assert_array_equal(ecu, cu_c)
+    np.testing.assert_allclose(ekc, kc, rtol=2 ** -7, atol=1e-6)
+    rows = g[f"{name}__rows"]
+    want = g[f"{name}__idx_rows"].astype(np.int32)
+    page_bits = g[f"{name}__page_bits"].view(np.uint16)
+    take = want.shape[-1]
+    page_at, ulp_flips, scored = 0, 0, 0
+    for b, n in enumerate(lens):
+        sel_rows = rows[(rows >= cu[b]) & (rows < cu[b + 1])]
+        c0, c1 = int(cu_c[b]), int(cu_c[b + 1])
+        pos = sel_rows - cu[b]
+        got = ora.select_for_queries(inputs.q[sel_rows], pos, n, kc[c0:c1], inputs.params,
+                                     take=take, init_blocks=init, local_blocks=local)
+        mine = np.isin(rows, sel_rows)
+        if c1 == c0:
+            assert np.all(want[:, mine] == -1)   # no atoms: the reference leaves -1
+            continue
+        # (3) end to end
+        bad = ora.selection_mismatches(want[:, mine], got, rel_tol=1e-3)
+        assert not bad, bad[:5]
+        # (1) the reference's page scores through the oracle's masking + top-k
+        prow = np.arange(0, len(sel_rows), 4)
+        p_count = (n + 63) // 64
+        ref_pages = ora.from_bf16_bits(page_bits[:, page_at:page_at + len(prow), :p_count])
+        page_at += len(prow)
+        from_ref = ora.select_from_scores(ref_pages, pos[prow], take=take, init_blocks=init,
+                                          local_blocks=local)
+        bad = ora.selection_mismatches(want[:, mine][:, prow], from_ref, rel_tol=1e-3)
+        assert not bad, bad[:5]
+        # (2) page scores, oracle vs reference: north_star's score tolerance,
+        # and almost all of them bit-identical
+        mine_pages = ora.score_pages(inputs.q[sel_rows[prow]], kc[c0:c1], inputs.params, seq_len=n,
+                                     policy="bf16")
+        vis = np.isfinite(ref_pages)
+        assert np.array_equal(np.isfinite(mine_pages), vis)
+        err = np.abs(mine_pages[vis] - ref_pages[vis])
+        assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())
+        ulp_flips += int(np.count_nonzero(err))
+        scored += int(vis.sum())
+    assert ulp_flips <= 0.02 * max(scored, 1), (ulp_flips, scored)

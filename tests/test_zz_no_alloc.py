@@ -68,10 +68,37 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(first, secon
     assert ops.check_status(DEV) == 0
 
 
+def test_noalloc_accepts_a_request_of_exactly_its_scratch():
+    """One 16384-token sequence with 2 KV groups needs exactly the 16 MiB built
+    into the library: accepted, and equal to the workspace entry point."""
+    from leanselect_b200.sweep import config1_layer, make_selector
+
+    n = 16384
+    lib = _native.load()
+    assert lib.ls_select_pages_workspace_bytes(n, 2, n) == 16 << 20
+    ops.status_word(DEV).zero_()
+    q, k, _ = config1_layer(n, DEV, 4)
+    w = make_selector(DEV, 4).kernel_weights()
+    cu = torch.tensor([0, n], dtype=torch.int32, device=DEV)
+    kc, cu_c = ops.compress_keys(k, cu, lengths=[n])
+    ks = ops.project_atom_keys(kc, w.wk_t)
+    for take in (67, 96):
+        out = torch.full((2, n, take), -7, dtype=torch.int32, device=DEV)
+        rc = lib.ls_select_pages_noalloc(
+            q.data_ptr(), w.wq_t.data_ptr(), ks.data_ptr(), cu.data_ptr(), cu_c.data_ptr(), 1, n,
+            n, ks.shape[1], 32, 2, 128, 128, take, 1, 2, 64, 16, out.data_ptr(),
+            ops.status_word(DEV).data_ptr(), torch.cuda.current_stream().cuda_stream)
+        assert rc == _native.LS_OK, lib.ls_last_error().decode()
+        want = ops.select_pages(q, w, ks, cu, cu_c, n, take=take)
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
+    assert ops.check_status(DEV) == 0
+
+
 def test_noalloc_rejects_requests_beyond_its_scratch():
     lib = _native.load()
     fake = ctypes.c_void_p(1 << 20)
-    # One 32K-token sequence needs 2 * 32768 * 512 * 4 bytes = 128 MiB of scratch.
+    # One 32K-token sequence needs 2 * 32768 * 512 * 2 bytes = 64 MiB of scratch.
     rc = lib.ls_select_pages_noalloc(fake, fake, fake, fake, fake, 1, 32768, 32768, 2047, 32, 2,
                                      128, 128, 67, 1, 2, 64, 16, fake, None, None)
     assert rc == _native.LS_ERR_UNSUPPORTED
