@@ -160,7 +160,7 @@ int ls_compress_keys(const uint16_t* k, const int32_t* cu_seqlens_k, int32_t bat
 int ls_project_atom_keys(const uint16_t* kc, int64_t total_c, int32_t num_kv_heads,
                          int32_t head_dim, const uint16_t* wk_t, int32_t width, uint16_t* ks,
                          void* stream) {
-  LS_REQUIRE(total_c >= 0, "bad total_c");
+  LS_REQUIRE(total_c >= 0 && total_c < (int64_t{1} << 31), "bad total_c");
   if (total_c == 0) return LS_OK;
   LS_REQUIRE(kc && wk_t && ks, "null argument");
   LS_REQUIRE(num_kv_heads > 0, "bad num_kv_heads");
@@ -168,8 +168,26 @@ int ls_project_atom_keys(const uint16_t* kc, int64_t total_c, int32_t num_kv_hea
     return fail(LS_ERR_UNSUPPORTED, "head_dim and selector width must be 128");
   LS_REQUIRE_ALIGNED(kc);
   LS_REQUIRE_ALIGNED(wk_t);
-  const cudaError_t err = launch_project_atom_keys(kc, total_c, num_kv_heads, wk_t, ks,
-                                                   static_cast<cudaStream_t>(stream));
+  LS_REQUIRE_ALIGNED(ks);
+  // The tcgen05 projection GEMM with one "head" per group: rows are atoms,
+  // Kc [total_c, G*D] plays the queries and wk_t [G*F, D] the folded weight.
+  ScoreArgs a{};
+  const uint64_t row = static_cast<uint64_t>(num_kv_heads) * 128;
+  if (!make_tensor_map_2d(&a.tm_q, kc, static_cast<uint64_t>(total_c), row, row * 2, 64, 128))
+    return fail(LS_ERR_CUDA, "cuTensorMapEncodeTiled failed for kc");
+  if (!make_tensor_map_2d(&a.tm_w, wk_t, row, 128, 256, 64, 128))
+    return fail(LS_ERR_CUDA, "cuTensorMapEncodeTiled failed for wk_t");
+  a.tm_ks = a.tm_w;  // unused by the projection
+  a.num_groups = num_kv_heads;
+  a.hg = 1;
+  a.total_q = total_c;
+  a.cu_q = nullptr;
+  a.cu_c = nullptr;
+  a.batch = 1;
+  a.max_seqlen_q = static_cast<int>(total_c);
+  a.qs_out = ks;
+  a.status = nullptr;
+  const cudaError_t err = launch_score(kModeProject, a, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? LS_OK : cuda_fail(err, "project_atom_keys launch");
 }
 
@@ -182,6 +200,7 @@ int check_score_common(const uint16_t* q, const uint16_t* wq_t, int64_t total_q,
   LS_REQUIRE(total_q >= 0 && total_q < (int64_t{1} << 31), "total_q out of range");
   LS_REQUIRE(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
              "num_heads must be a positive multiple of num_kv_heads");
+  LS_REQUIRE(total_q * num_kv_heads < (int64_t{1} << 31), "num_kv_heads * total_q out of range");
   if (head_dim != 128 || width != 128)
     return fail(LS_ERR_UNSUPPORTED, "head_dim and selector width must be 128");
   const int hg = num_heads / num_kv_heads;
@@ -394,6 +413,7 @@ int ls_uniform_select_pages(const uint16_t* q, const uint16_t* kc, const int32_t
   LS_REQUIRE(total_q >= 0 && total_q < (int64_t{1} << 31), "total_q out of range");
   LS_REQUIRE(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
              "num_heads must be a positive multiple of num_kv_heads");
+  LS_REQUIRE(total_q * num_kv_heads < (int64_t{1} << 31), "num_kv_heads * total_q out of range");
   if (head_dim != 128) return fail(LS_ERR_UNSUPPORTED, "head_dim must be 128");
   const int hg = num_heads / num_kv_heads;
   if (hg != 8 && hg != 16) return fail(LS_ERR_UNSUPPORTED, "heads per group must be 8 or 16");

@@ -22,9 +22,6 @@ cudaError_t launch_compress_keys(const uint16_t* k, const int32_t* cu_k, const i
                                  int kernel_size, int kernel_stride, uint16_t* kc,
                                  int32_t* status, cudaStream_t stream);
 
-cudaError_t launch_project_atom_keys(const uint16_t* kc, int64_t total_c, int G,
-                                     const uint16_t* wk_t, uint16_t* ks, cudaStream_t stream);
-
 // Score/select kernel family (score_select.cu).
 enum ScoreMode { kModeProject = 0, kModeScore = 1, kModeSelect = 2, kModeAtoms = 3 };
 

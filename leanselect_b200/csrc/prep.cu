@@ -165,68 +165,6 @@ __global__ void __launch_bounds__(256) compress_keys_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Atom-key projection (selector.py:179-190): Ks[g, a, f] = sum_d Kc[a, g, d] Wk[g, f, d]
-// ---------------------------------------------------------------------------
-
-constexpr int kProjAtoms = 32;
-
-__global__ void __launch_bounds__(256) project_atom_keys_kernel(
-    const __nv_bfloat16* __restrict__ kc, int64_t total_c, int G, const __nv_bfloat16* __restrict__ wk_t,
-    __nv_bfloat16* __restrict__ ks) {
-  // D = F = 128.  Padded rows keep the 16-byte reads of W conflict-free.
-  constexpr int D = 128, F = 128, WP = D + 8;
-  __shared__ __align__(16) __nv_bfloat16 w_s[F * WP];
-  __shared__ __align__(16) __nv_bfloat16 k_s[kProjAtoms * D];
-  const int g = blockIdx.y;
-  const int64_t a0 = static_cast<int64_t>(blockIdx.x) * kProjAtoms;
-  for (int i = threadIdx.x; i < F * D / 8; i += blockDim.x) {
-    const int f = i / (D / 8), c = i % (D / 8);
-    *reinterpret_cast<uint4*>(&w_s[f * WP + c * 8]) =
-        *reinterpret_cast<const uint4*>(&wk_t[(static_cast<int64_t>(g) * F + f) * D + c * 8]);
-  }
-  for (int i = threadIdx.x; i < kProjAtoms * D / 8; i += blockDim.x) {
-    const int a = i / (D / 8), c = i % (D / 8);
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (a0 + a < total_c)
-      v = *reinterpret_cast<const uint4*>(&kc[((a0 + a) * G + g) * D + c * 8]);
-    *reinterpret_cast<uint4*>(&k_s[a * D + c * 8]) = v;
-  }
-  __syncthreads();
-  const int f = threadIdx.x & (F - 1);
-  const int abase = (threadIdx.x >> 7) * (kProjAtoms / 2);
-  float acc[kProjAtoms / 2];
-#pragma unroll
-  for (int i = 0; i < kProjAtoms / 2; ++i) acc[i] = 0.f;
-  for (int d = 0; d < D; d += 8) {
-    const uint4 wv = *reinterpret_cast<const uint4*>(&w_s[f * WP + d]);
-    const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wv);
-    float w[8];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const float2 t = __bfloat1622float2(wh[c]);
-      w[2 * c] = t.x;
-      w[2 * c + 1] = t.y;
-    }
-#pragma unroll
-    for (int i = 0; i < kProjAtoms / 2; ++i) {
-      const uint4 kv = *reinterpret_cast<const uint4*>(&k_s[(abase + i) * D + d]);
-      const __nv_bfloat162* kh = reinterpret_cast<const __nv_bfloat162*>(&kv);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float2 t = __bfloat1622float2(kh[c]);
-        acc[i] = fmaf(t.x, w[2 * c], acc[i]);
-        acc[i] = fmaf(t.y, w[2 * c + 1], acc[i]);
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < kProjAtoms / 2; ++i) {
-    const int64_t a = a0 + abase + i;
-    if (a < total_c) ks[(static_cast<int64_t>(g) * total_c + a) * F + f] = __float2bfloat16_rn(acc[i]);
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Uniform method inputs (ops/uniform.py, pages.py:62-71)
 // ---------------------------------------------------------------------------
 
@@ -315,14 +253,5 @@ cudaError_t launch_compress_keys(const uint16_t* k, const int32_t* cu_k, const i
   return cudaGetLastError();
 }
 
-cudaError_t launch_project_atom_keys(const uint16_t* kc, int64_t total_c, int G,
-                                     const uint16_t* wk_t, uint16_t* ks, cudaStream_t stream) {
-  if (total_c == 0) return cudaSuccess;
-  dim3 grid(static_cast<unsigned>((total_c + kProjAtoms - 1) / kProjAtoms), G);
-  project_atom_keys_kernel<<<grid, 256, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(kc), total_c, G,
-      reinterpret_cast<const __nv_bfloat16*>(wk_t), reinterpret_cast<__nv_bfloat16*>(ks));
-  return cudaGetLastError();
-}
 
 }  // namespace ls

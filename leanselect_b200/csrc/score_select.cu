@@ -501,16 +501,17 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
 // Top-T' page selection per (group, row)
 // ---------------------------------------------------------------------------
 
-constexpr int kTopkWarps = 8;
+constexpr int kTopkWarps = 4;
+constexpr int kTopkBlocksPerSm = 7;        // 7 x 4 warps x 7.2 KB of shared memory per SM
 constexpr int kRowCap = 2048;              // candidates a warp stages in shared memory
 constexpr int kRowChunks = kRowCap / 8 + 1;  // 16-byte chunks, +1 for a misaligned start
-constexpr int kKeptCap = 256;              // candidates kept above the estimated cut
+constexpr int kKeptCap = 512;              // candidates kept above the estimated cut
 
 struct TopkWarpSmem {
   uint4 row[kRowChunks];        // the row's candidate scores (bf16), 16-byte aligned copy
   uint32_t hist[256];           // radix / sample histograms
-  uint16_t kept_key[kKeptCap];  // candidates at or above the cut, in candidate order
-  uint16_t kept_idx[kKeptCap];
+  uint32_t kept[kKeptCap];      // candidates at or above the cut, in candidate order:
+                                // key << 16 | candidate index
 };
 
 constexpr size_t topk_smem_bytes() { return kTopkWarps * sizeof(TopkWarpSmem); }
@@ -523,6 +524,8 @@ __device__ __forceinline__ uint32_t bf16_key(uint32_t b) {
   const uint32_t k = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
   return (k <= 0x7Fu || k > 0xFF80u) ? 0u : k;
 }
+
+__device__ __forceinline__ float bf16_value(uint32_t b) { return __uint_as_float(b << 16); }
 
 __device__ __forceinline__ uint32_t chunk_bits(const uint4& v, int e) {
   const uint32_t w = e < 2 ? v.x : e < 4 ? v.y : e < 6 ? v.z : v.w;
@@ -554,8 +557,8 @@ struct ChunkKeys {        // key of candidate i
   __device__ __forceinline__ uint32_t operator()(int i) const { return bf16_key(src.bits(off + i)); }
 };
 struct KeptKeys {         // entry j of the warp's kept buffer
-  const uint16_t* k;
-  __device__ __forceinline__ uint32_t operator()(int j) const { return k[j]; }
+  const uint32_t* k;
+  __device__ __forceinline__ uint32_t operator()(int j) const { return k[j] >> 16; }
 };
 
 // Exclusive prefix sum over the warp; returns it and sets `total`.
@@ -571,21 +574,40 @@ __device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
 }
 
 // Exact threshold of the `need` largest nonzero 16-bit keys among
-// keys(0 .. count-1): MSB-first radix select, 2 passes of 8 bits over a warp
-// histogram in shared memory.  Returns the threshold key; `need` becomes the
-// number of keys equal to it that belong to the selection (lowest indices win).
+// keys(0 .. count-1), need >= 1.  A histogram over the keys' own range:
+// 256 bins of width 2^shift from the smallest key, so one pass is exact
+// when the keys span fewer than 256 values and a second pass over the bin
+// that holds the threshold finishes otherwise.  Returns the threshold key;
+// `need` becomes the number of keys equal to it that belong to the
+// selection (the lowest indices win).
 template <class Keys>
 __device__ uint32_t radix_threshold16(const Keys& keys, int count, int& need, uint32_t* hist,
                                       int lane) {
-  uint32_t prefix = 0, mask = 0;
+  uint32_t kmin = 0xFFFFu, kmax = 0u;
+  for (int i = lane; i < count; i += 32) {
+    const uint32_t key = keys(i);
+    if (key != 0u) {
+      kmin = min(kmin, key);
+      kmax = max(kmax, key);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+  }
+  const uint32_t range = kmax - kmin;
+  int shift = range > 255u ? (32 - __clz(range)) - 8 : 0;  // (range >> shift) < 256
+  uint32_t lo = kmin;        // keys of the current pass: [lo, lo + (256 << shift))
+  uint32_t width = 256u << shift;
 #pragma unroll 1
-  for (int pass = 0; pass < 2; ++pass) {
-    const int shift = 8 - 8 * pass;
-    for (int k = lane; k < 256; k += 32) hist[k] = 0;
+  while (true) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hist[lane + 32 * j] = 0;
     __syncwarp();
     for (int i = lane; i < count; i += 32) {
       const uint32_t key = keys(i);
-      if (key != 0u && ((key ^ prefix) & mask) == 0) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      if (key != 0u && key >= lo && key - lo < width) atomicAdd(&hist[(key - lo) >> shift], 1u);
     }
     __syncwarp();
     // Lane l owns bins 255-8l .. 248-8l (descending).
@@ -623,11 +645,12 @@ __device__ uint32_t radix_threshold16(const Keys& keys, int count, int& need, ui
     bin = __shfl_sync(0xffffffffu, bin, owner);
     above = __shfl_sync(0xffffffffu, above, owner);
     need -= static_cast<int>(above);
-    prefix |= static_cast<uint32_t>(bin) << shift;
-    mask |= 0xFFu << shift;
     __syncwarp();
+    lo += static_cast<uint32_t>(bin) << shift;
+    if (shift == 0) return lo;
+    width = 1u << shift;   // the bin's keys, one per bin in the next pass
+    shift = 0;
   }
-  return prefix;
 }
 
 // Writes, in index order, the entries among keys(0 .. count-1) above `thr`
@@ -659,37 +682,51 @@ struct Identity {
   __device__ __forceinline__ int operator()(int j) const { return j; }
 };
 struct KeptIndex {
-  const uint16_t* idx;
-  __device__ __forceinline__ int operator()(int j) const { return idx[j]; }
+  const uint32_t* k;
+  __device__ __forceinline__ int operator()(int j) const { return static_cast<int>(k[j] & 0xFFFFu); }
 };
 
-// One pass over candidates 0 .. m-1 in rounds of 32 chunks (lane l takes
-// chunk base + l, eight candidates); candidates whose key satisfies `pred`
-// are handed to `emit(pos, key, i)` with consecutive positions in candidate
-// order.  Returns how many were emitted.
-template <class Src, class Pred, class Emit>
-__device__ int compact_candidates(const Src& src, int off, int m, const Pred& pred, const Emit& emit,
-                                  int lane) {
+__device__ __forceinline__ __nv_bfloat162 as_bf162(uint32_t w) {
+  return *reinterpret_cast<const __nv_bfloat162*>(&w);
+}
+
+// Flags (bit e) of the candidates of a 16-byte chunk whose score is >= cut:
+// two bf16 compares per instruction; NaN never passes.
+__device__ __forceinline__ uint32_t chunk_ge_flags(const uint4& v, __nv_bfloat162 cut) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t flags = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t mk = __hge2_mask(as_bf162(w[j]), cut);   // 0xFFFF per passing half
+    flags |= ((mk & 1u) | ((mk >> 15) & 2u)) << (2 * j);
+  }
+  return flags;
+}
+
+// One pass over candidates 0 .. m-1 in rounds of 64 chunks (lane l takes
+// chunks base + 2l and base + 2l + 1, sixteen consecutive candidates): the
+// candidates whose score is >= `cut` are handed to `emit(pos, bits, i)`
+// with consecutive positions in candidate order (`bits(e)` of the source
+// re-reads a passing score).  Returns how many there were.
+template <class Src, class Emit>
+__device__ int compact_ge(const Src& src, int off, int m, __nv_bfloat162 cut, const Emit& emit,
+                          int lane) {
   const int nch = (off + m + 7) >> 3;
   int total = 0;
-  for (int base = 0; base < nch; base += 32) {
-    const int c = base + lane;
-    const uint4 v = c < nch ? src.chunk(c) : make_uint4(0u, 0u, 0u, 0u);
-    uint32_t keys[8];
-    int mine = 0;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int i = 8 * c + e - off;
-      const uint32_t key = bf16_key(chunk_bits(v, e));
-      keys[e] = (i >= 0 && i < m && pred(key, i)) ? key : 0u;
-      mine += keys[e] != 0u ? 1 : 0;
-    }
+  for (int base = 0; base < nch; base += 64) {
+    const int c = base + 2 * lane;
+    uint32_t flags = 0;  // bit e: candidate 8c - off + e passes
+    if (c < nch) flags = chunk_ge_flags(src.chunk(c), cut);
+    if (c + 1 < nch) flags |= chunk_ge_flags(src.chunk(c + 1), cut) << 8;
+    const int first = 8 * c - off;  // candidate index of bit 0
+    if (first < 0) flags &= 0xFFFFu << (-first);
+    if (first + 16 > m) flags &= m - first <= 0 ? 0u : (0xFFFFu >> (16 - (m - first)));
     int round_total;
-    int pos = total + warp_excl_scan(mine, lane, round_total);
-    if (mine) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (keys[e] != 0u) emit(pos++, keys[e], 8 * c + e - off);
+    int pos = total + warp_excl_scan(__popc(flags), lane, round_total);
+    while (flags) {
+      const int e = __ffs(flags) - 1;
+      flags &= flags - 1;
+      emit(pos++, src.bits(8 * c + e), first + e);
     }
     total += round_total;
   }
@@ -700,25 +737,32 @@ __device__ int compact_candidates(const Src& src, int off, int m, const Pred& pr
 // candidate index) and writes their pages (n_init + i) to out[k_out ...] in
 // ascending order.  Returns the next output position.
 //
-// Candidates with keys at or above a cut estimated from a 1/8 sample
-// (every 8th round of chunks; a 128-bin histogram over the sample's key
-// range, aiming at ~1.5x the needed count) go to the warp's kept buffer in
-// one pass; the exact radix select then runs over those.  When the estimate
-// kept too few or too many, the exact radix runs over the whole row.
-template <class Src>
-__device__ int select_row(const Src& src, int off, int m, int cap, int skip, int n_init,
-                          int32_t* out, int k_out, TopkWarpSmem* ws, int lane) {
+// Candidates at or above a cut estimated from a 1/8 sample (every 8th
+// round of chunks; a 128-bin histogram linear in value between the sample's
+// min and max, aiming at ~2.5x the needed count) go to the warp's kept
+// buffer in one pass; the exact radix select then runs over those.  When
+// the estimate kept too few or too many, the exact radix runs over the
+// whole row, read from the workspace (`row`).  `release()` is called once
+// `src` will not be read again (its shared-memory copy may then be reused).
+template <class Src, class Release>
+__device__ int select_row(const Src& src, const GlobalChunks& row, int off, int m, int cap, int skip,
+                          int n_init, int32_t* out, int k_out, TopkWarpSmem* ws,
+                          const Release& release, int lane) {
   if (cap <= 0 || m <= 0) return k_out;
-  const ChunkKeys<Src> row_keys{src, off};
+  // Every finite candidate selected: the skipped one (always the last) is
+  // left out of the range, so it takes no output position.
+  const __nv_bfloat162 finite2 = as_bf162(0xFF7FFF7Fu);  // lowest finite bf16, twice
+  const int m_out = skip >= 0 ? skip : m;
+  const auto write_out = [&](int pos, uint32_t, int i) { out[k_out + pos] = n_init + i; };
   if (cap >= m) {
-    // Every finite candidate is selected.
-    return k_out + compact_candidates(
-                       src, off, m, [&](uint32_t key, int i) { return key != 0u && i != skip; },
-                       [&](int pos, uint32_t, int i) { out[k_out + pos] = n_init + i; }, lane);
+    k_out += compact_ge(src, off, m_out, finite2, write_out, lane);
+    __syncwarp();
+    release();
+    return k_out;
   }
-  // ---- 1/8 sample: key range and count.
+  // ---- 1/8 sample: value range and count of the finite sampled scores.
   const int nch = (off + m + 7) >> 3;
-  uint32_t kmin = 0xFFFFu, kmax = 0u;
+  float smin = INFINITY, smax = -INFINITY;
   int sampled = 0;
   for (int base = 0; base < nch; base += 256) {
     const int c = base + lane;
@@ -729,10 +773,10 @@ __device__ int select_row(const Src& src, int off, int m, int cap, int skip, int
         const int i = 8 * c + e - off;
         if (i >= 0 && i < m) {
           ++sampled;
-          const uint32_t key = bf16_key(chunk_bits(v, e));
-          if (key != 0u) {
-            kmin = min(kmin, key);
-            kmax = max(kmax, key);
+          const float x = bf16_value(chunk_bits(v, e));
+          if (x > -INFINITY && x < INFINITY) {
+            smin = fminf(smin, x);
+            smax = fmaxf(smax, x);
           }
         }
       }
@@ -741,15 +785,18 @@ __device__ int select_row(const Src& src, int off, int m, int cap, int skip, int
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     sampled += __shfl_xor_sync(0xffffffffu, sampled, o);
-    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
-    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    smin = fminf(smin, __shfl_xor_sync(0xffffffffu, smin, o));
+    smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
   }
-  uint32_t cut = 1u;  // keep every finite key unless the sample says better
-  if (kmax > kmin) {
-    const uint32_t range = kmax - kmin;
-    const int shift = range > 127u ? (32 - __clz(range)) - 7 : 0;  // (range >> shift) < 128
+  // The cut: the lower edge of the bin of a 128-bin histogram, linear in
+  // value between the sample's min and max, where the count from the top
+  // reaches ~1.5 cap * sampled / m.  -inf keeps every finite candidate.
+  float cut = -INFINITY;
+  if (smax > smin) {
+    const float scale = 128.f / (smax - smin);
     uint32_t* hist = ws->hist;
-    for (int k = lane; k < 128; k += 32) hist[k] = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) hist[lane + 32 * j] = 0;
     __syncwarp();
     for (int base = 0; base < nch; base += 256) {
       const int c = base + lane;
@@ -758,13 +805,16 @@ __device__ int select_row(const Src& src, int off, int m, int cap, int skip, int
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int i = 8 * c + e - off;
-          const uint32_t key = bf16_key(chunk_bits(v, e));
-          if (i >= 0 && i < m && key != 0u) atomicAdd(&hist[(key - kmin) >> shift], 1u);
+          const float x = bf16_value(chunk_bits(v, e));
+          if (i >= 0 && i < m && x > -INFINITY && x < INFINITY)
+            atomicAdd(&hist[min(127, static_cast<int>((x - smin) * scale))], 1u);
         }
       }
     }
     __syncwarp();
-    const int target = max(1, min(sampled, static_cast<int>(1.5f * cap * sampled / m) + 1));
+    // ~2.5x the needed count: the kept count then falls short of cap (and
+    // the whole row is searched) for well under 1% of rows.
+    const int target = max(1, min(sampled, static_cast<int>(2.5f * cap * sampled / m) + 2));
     uint32_t c4[4];
     uint32_t lane_sum = 0;
 #pragma unroll
@@ -795,139 +845,187 @@ __device__ int select_row(const Src& src, int off, int m, int cap, int skip, int
     }
     if (owner_mask != 0u) {
       bin = __shfl_sync(0xffffffffu, bin, __ffs(owner_mask) - 1);
-      cut = max(1u, kmin + (static_cast<uint32_t>(bin) << shift));
+      // A candidate of bin b >= bin has (x - smin) * scale >= bin, so x is at
+      // least this edge up to one rounding; stepping one ulp down keeps it.
+      cut = bin > 0 ? nextafterf(smin + static_cast<float>(bin) / scale, -INFINITY) : -INFINITY;
     }
     __syncwarp();
   }
   // ---- one pass: keep the candidates at or above the cut, in candidate order.
-  const int kept = compact_candidates(
-      src, off, m, [&](uint32_t key, int) { return key >= cut; },
-      [&](int pos, uint32_t key, int i) {
-        if (pos < kKeptCap) {
-          ws->kept_key[pos] = static_cast<uint16_t>(key);
-          ws->kept_idx[pos] = static_cast<uint16_t>(i);
-        }
+  // A bf16 score is >= cut iff it is >= cut rounded up to bf16.
+  const uint32_t cut_bits =
+      cut > -INFINITY ? static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_ru(cut)))
+                      : 0xFF7Fu;
+  const int kept = compact_ge(
+      src, off, m, as_bf162(cut_bits | (cut_bits << 16)),
+      [&](int pos, uint32_t bits, int i) {
+        if (pos < kKeptCap) ws->kept[pos] = bf16_key(bits) << 16 | static_cast<uint32_t>(i);
       },
       lane);
   __syncwarp();
+  release();
   int need = cap;
   if (kept >= cap && kept <= kKeptCap) {
-    const KeptKeys kk{ws->kept_key};
+    const KeptKeys kk{ws->kept};
     const uint32_t thr = radix_threshold16(kk, kept, need, ws->hist, lane);
-    return emit_threshold(kk, KeptIndex{ws->kept_idx}, kept, thr, need, skip, n_init, out, k_out,
-                          lane);
+    return emit_threshold(kk, KeptIndex{ws->kept}, kept, thr, need, skip, n_init, out, k_out, lane);
   }
   // ---- exact radix over the whole row (the estimate kept too few or too many).
+  const ChunkKeys<GlobalChunks> row_keys{row, off};
   int finite = 0;
   for (int i = lane; i < m; i += 32) finite += row_keys(i) != 0u;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) finite += __shfl_xor_sync(0xffffffffu, finite, o);
-  if (finite <= cap) {
-    return k_out + compact_candidates(
-                       src, off, m, [&](uint32_t key, int i) { return key != 0u && i != skip; },
-                       [&](int pos, uint32_t, int i) { out[k_out + pos] = n_init + i; }, lane);
-  }
+  if (finite <= cap) return k_out + compact_ge(row, off, m_out, finite2, write_out, lane);
   const uint32_t thr = radix_threshold16(row_keys, m, need, ws->hist, lane);
   return emit_threshold(row_keys, Identity{}, m, thr, need, skip, n_init, out, k_out, lane);
 }
 
+// Geometry of one (group, query) row of the top-k kernel (minicpm.py:3121-3138).
+struct RowPlan {
+  bool valid;           // a row to process
+  bool empty;           // the row stays all -1 (bad seqlens, or no atoms outside uniform)
+  int32_t* out;
+  const uint4* row4;    // the candidates' 16-byte chunks in the workspace
+  int off, nch;         // candidate i is element off + i of nch chunks
+  int m_all, cap, future, n_init, take_b, local0, n_local;
+  bool staged;          // copied into the warp's shared memory
+};
+
+__device__ __forceinline__ RowPlan plan_row(const ScoreArgs& args, uint32_t r, uint32_t total_q,
+                                            uint32_t rows_total) {
+  RowPlan p{};
+  p.valid = r < rows_total;
+  if (!p.valid) return p;
+  const int64_t q_row = r % total_q;
+  p.out = args.topk_idx + static_cast<int64_t>(r) * args.take;
+  int b = 0, n;
+  int64_t q0 = 0;
+  if (args.cu_q) {
+    b = find_sequence(args.cu_q, args.batch, q_row);
+    q0 = __ldg(args.cu_q + b);
+    n = static_cast<int>(__ldg(args.cu_q + b + 1) - q0);
+    if (n > args.max_seqlen_q) {  // reported by score_kernel; the row stays empty
+      p.empty = true;
+      return p;
+    }
+  } else {
+    n = args.max_seqlen_q;
+  }
+  const int atoms = args.cu_c ? static_cast<int>(__ldg(args.cu_c + b + 1) - __ldg(args.cu_c + b))
+                              : static_cast<int>(args.total_c);
+  const int pos = args.pos_offset + static_cast<int>(q_row - q0);
+  const int pages = ((args.seq_len > 0 ? args.seq_len : n) + 63) / 64;
+  const int qp = pos / 64;
+  p.take_b = min(args.take, pages);
+  p.n_init = min(args.init_blocks, qp + 1);             // sink pages 0 .. n_init-1
+  const int lo = max(0, qp - args.local_blocks);         // local pages lo .. qp
+  p.local0 = max(lo, p.n_init);
+  p.n_local = qp - p.local0 + 1;                         // local pages that are not sinks
+  int m = max(0, lo - p.n_init);                         // candidates n_init .. lo-1
+  int slots = p.take_b - (p.n_init + p.n_local);
+  // Uniform method: page qp+1 is scored too (its first window atom may be
+  // visible) and competes as candidate m, or as a forced sink; either way
+  // a slot it wins stays -1 (uniform.py:100-106).  Rows of sequences
+  // without atoms keep their forced pages (head_mix.py:150-170).
+  p.future = -1;
+  if (args.uniform) {
+    if (atoms <= 0) m = 0;
+    slots -= max(0, min(args.init_blocks, pages) - (qp + 1));  // future sinks
+    if (atoms > 0 && qp + 1 < pages && qp + 1 >= args.init_blocks) p.future = m;
+  } else if (atoms <= 0) {
+    // The reference leaves rows of sequences without atoms at -1 (minicpm.py:3115-3116).
+    p.empty = true;
+    return p;
+  }
+  p.m_all = m + (p.future >= 0 ? 1 : 0);
+  p.cap = max(0, min(slots, p.m_all));
+  // Candidate i is page n_init + i; candidate m (page qp+1) was stored by
+  // the score kernel in slot n_init + m, the first non-sink local page.
+  // Chunks start at the 8-page boundary below the first candidate (rows are
+  // 16-byte aligned).
+  p.off = p.n_init & 7;
+  p.row4 = reinterpret_cast<const uint4*>(args.workspace + static_cast<int64_t>(r) * args.max_pages) +
+           (p.n_init >> 3);
+  p.nch = (p.off + p.m_all + 7) >> 3;
+  p.staged = p.cap > 0 && p.nch <= kRowChunks;
+  return p;
+}
+
+// Starts the asynchronous 16-byte copies of a staged row into the warp's
+// shared memory (no registers held, all of a lane's copies in flight).
+__device__ __forceinline__ void stage_row(const RowPlan& p, TopkWarpSmem* ws, int lane) {
+  if (!p.valid || !p.staged) return;
+  for (int c = lane; c < p.nch; c += 32) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(ws->row + c)),
+                 "l"(p.row4 + c)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 // Top-T' of each (group, query) row, one warp per row.  A row's candidate
 // scores are bf16 values of the workspace; rows of at most kRowCap
-// candidates are first copied into the warp's shared memory with 16-byte
-// loads (all in flight at once), longer rows are read from the workspace.
-// The result is the same on every path: the T' largest scores, ties to the
+// candidates are copied into the warp's shared memory, longer rows are read
+// from the workspace.  The copy of a warp's next row starts as soon as the
+// current row's copy is no longer read (after its filtering pass), so it
+// overlaps the exact selection and the output of the current row.  The
+// result is the same on every path: the T' largest scores, ties to the
 // lower page.
-__global__ void __launch_bounds__(kTopkWarps * 32, 4) topk_kernel(const __grid_constant__ ScoreArgs args) {
+__global__ void __launch_bounds__(kTopkWarps * 32, kTopkBlocksPerSm) topk_kernel(const __grid_constant__ ScoreArgs args) {
   extern __shared__ __align__(16) uint8_t topk_smem_raw[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   TopkWarpSmem* ws = reinterpret_cast<TopkWarpSmem*>(topk_smem_raw) + warp;
-  const int64_t rows_total = static_cast<int64_t>(args.num_groups) * args.total_q;
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kTopkWarps + warp; r < rows_total;
-       r += static_cast<int64_t>(gridDim.x) * kTopkWarps) {
-    const int64_t q_row = r % args.total_q;
-    int b = 0, n;
-    int64_t q0 = 0;
-    if (args.cu_q) {
-      b = find_sequence(args.cu_q, args.batch, q_row);
-      q0 = __ldg(args.cu_q + b);
-      n = static_cast<int>(__ldg(args.cu_q + b + 1) - q0);
-      if (n > args.max_seqlen_q) {  // reported by score_kernel; the row stays empty
-        for (int k = lane; k < args.take; k += 32) args.topk_idx[r * args.take + k] = -1;
-        continue;
+  // Rows r = g * total_q + q_row with G * total_q < 2^31 (host checks), so
+  // 32-bit unsigned arithmetic indexes them without wrapping.
+  const uint32_t total_q = static_cast<uint32_t>(args.total_q);
+  const uint32_t rows_total = static_cast<uint32_t>(args.num_groups) * total_q;
+  const uint32_t stride = gridDim.x * kTopkWarps;
+  uint32_t r = blockIdx.x * kTopkWarps + warp;
+  RowPlan cur = plan_row(args, r, total_q, rows_total);
+  stage_row(cur, ws, lane);
+  while (cur.valid) {
+    const RowPlan nxt = plan_row(args, r + stride, total_q, rows_total);
+    bool next_staged = false;
+    const auto release = [&]() {
+      if (!next_staged) {
+        next_staged = true;
+        stage_row(nxt, ws, lane);
       }
-    } else {
-      n = args.max_seqlen_q;
-    }
-    const int atoms = args.cu_c ? static_cast<int>(__ldg(args.cu_c + b + 1) - __ldg(args.cu_c + b))
-                                : static_cast<int>(args.total_c);
-    const int pos = args.pos_offset + static_cast<int>(q_row - q0);
-    const int pages = ((args.seq_len > 0 ? args.seq_len : n) + 63) / 64;
-    int32_t* out = args.topk_idx + r * args.take;
-    const uint16_t* scores = args.workspace + r * args.max_pages;
-
-    // Row geometry (minicpm.py:3121-3138).
-    const int qp = pos / 64;
-    const int take_b = min(args.take, pages);
-    const int n_init = min(args.init_blocks, qp + 1);   // sink pages 0 .. n_init-1
-    const int lo = max(0, qp - args.local_blocks);       // local pages lo .. qp
-    const int local0 = max(lo, n_init);
-    const int n_local = qp - local0 + 1;                 // local pages that are not sinks
-    const int n_forced = n_init + n_local;
-    int m = max(0, lo - n_init);                         // candidates n_init .. lo-1
-    int slots = take_b - n_forced;
-    // Uniform method: page qp+1 is scored too (its first window atom may be
-    // visible) and competes as candidate m, or as a forced sink; either way
-    // a slot it wins stays -1 (uniform.py:100-106).  Rows of sequences
-    // without atoms keep their forced pages (head_mix.py:150-170).
-    int future = -1;
-    if (args.uniform) {
-      if (atoms <= 0) m = 0;
-      slots -= max(0, min(args.init_blocks, pages) - (qp + 1));  // future sinks
-      if (atoms > 0 && qp + 1 < pages && qp + 1 >= args.init_blocks) future = m;
-    } else if (atoms <= 0) {
-      // The reference leaves rows of sequences without atoms at -1 (minicpm.py:3115-3116).
+    };
+    int32_t* out = cur.out;
+    if (cur.empty) {
       for (int k = lane; k < args.take; k += 32) out[k] = -1;
-      continue;
-    }
-    const int m_all = m + (future >= 0 ? 1 : 0);
-    const int cap = max(0, min(slots, m_all));
-    // Candidate i is page n_init + i; candidate m (page qp+1) was stored by
-    // the score kernel in slot n_init + m, the first non-sink local page.
-    const int sinks_out = min(n_init, take_b);
-    for (int k = lane; k < sinks_out; k += 32) out[k] = k;
-    int k_out = sinks_out;
-
-    if (cap > 0) {
-      // Chunks start at the 8-page boundary below the first candidate (rows
-      // are 16-byte aligned); candidate i is element off + i.
-      const int off = n_init & 7;
-      const uint4* row4 = reinterpret_cast<const uint4*>(scores) + (n_init >> 3);
-      const int nch = (off + m_all + 7) >> 3;
-      if (nch <= kRowChunks) {
-        // Copy the row into shared memory with asynchronous 16-byte copies
-        // (no registers held, every copy of the lane in flight at once).
-        for (int c = lane; c < nch; c += 32) {
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(ws->row + c)),
-                       "l"(row4 + c)
-                       : "memory");
+    } else {
+      const int sinks_out = min(cur.n_init, cur.take_b);
+      for (int k = lane; k < sinks_out; k += 32) out[k] = k;
+      int k_out = sinks_out;
+      if (cur.cap > 0) {
+        const GlobalChunks row{cur.row4};
+        if (cur.staged) {
+          asm volatile("cp.async.wait_all;" ::: "memory");
+          __syncwarp();
+          k_out = select_row(SmemChunks{ws->row}, row, cur.off, cur.m_all, cur.cap, cur.future,
+                             cur.n_init, out, k_out, ws, release, lane);
+        } else {
+          k_out = select_row(row, row, cur.off, cur.m_all, cur.cap, cur.future, cur.n_init, out,
+                             k_out, ws, release, lane);
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
         __syncwarp();
-        k_out = select_row(SmemChunks{ws->row}, off, m_all, cap, future, n_init, out, k_out, ws,
-                           lane);
-      } else {
-        k_out = select_row(GlobalChunks{row4}, off, m_all, cap, future, n_init, out, k_out, ws,
-                           lane);
       }
-      __syncwarp();
+      // Local pages (those that are not sinks), then padding.
+      const int local_out = max(0, min(cur.n_local, cur.take_b - k_out));
+      for (int k = lane; k < local_out; k += 32) out[k_out + k] = cur.local0 + k;
+      k_out += local_out;
+      for (int k = k_out + lane; k < args.take; k += 32) out[k] = -1;
     }
-    // Local pages (those that are not sinks), then padding.
-    const int local_out = max(0, min(n_local, take_b - k_out));
-    for (int k = lane; k < local_out; k += 32) out[k_out + k] = local0 + k;
-    k_out += local_out;
-    for (int k = k_out + lane; k < args.take; k += 32) out[k] = -1;
+    __syncwarp();
+    release();
+    cur = nxt;
+    r += stride;
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 }  // namespace
@@ -972,7 +1070,8 @@ cudaError_t launch_score(int mode, const ScoreArgs& args_in, cudaStream_t stream
       err = cudaGetLastError();
       if (err != cudaSuccess) return err;
       const int64_t rows = static_cast<int64_t>(args.num_groups) * args.total_q;
-      const int64_t blocks = std::min<int64_t>((rows + kTopkWarps - 1) / kTopkWarps, 148 * 16);
+      const int64_t blocks =
+          std::min<int64_t>((rows + kTopkWarps - 1) / kTopkWarps, 148 * kTopkBlocksPerSm * 4);
       err = cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(topk_smem_bytes()));
       if (err != cudaSuccess) return err;
