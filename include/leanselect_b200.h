@@ -274,6 +274,8 @@ int ls_select_pages_chunk(const uint16_t* q, const uint16_t* wq_t, const uint16_
  * (lse = +inf).  q [total_q, H, D], k/v [total_k, G, D], out [total_q, H, D]
  * bf16; lse [H, total_q] fp32 (nullable); scale <= 0 selects D^-0.5.
  * Requires D == 128, H/G in {8, 16}, block_size == 64, topk <= LS_MAX_TOPK.
+ * When the status word reports LS_DEVERR_TIMEOUT, the rows whose CTA gave
+ * up are left unwritten in out and lse (their contents are undefined).
  */
 int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                    const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t batch,
@@ -298,6 +300,18 @@ int ls_sparse_attn_gather_only(const uint16_t* q, const uint16_t* k, const uint1
                                int32_t num_kv_heads, int32_t head_dim, const int32_t* topk_idx,
                                int32_t topk, int32_t block_size, int32_t causal, int32_t* status,
                                void* stream);
+
+/*
+ * ls_wait_timeout_probe -- test hook for the bounded waits (no reference
+ * counterpart).  Launches one CTA that allocates tensor memory and waits on
+ * an mbarrier that nothing completes, for timeout_ns (1 us .. 2 s), then
+ * unwinds the way every kernel of this library does when a wait expires:
+ * LS_DEVERR_TIMEOUT is OR-ed into *status (device int32), the other warps
+ * leave through the CTA's abort flag, the tensor memory is released and the
+ * kernel returns, writing 1 to *done (device int32).  The context stays
+ * usable; nothing traps.
+ */
+int ls_wait_timeout_probe(int32_t* status, int32_t* done, uint64_t timeout_ns, void* stream);
 
 #ifdef __cplusplus
 }

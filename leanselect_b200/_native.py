@@ -56,6 +56,7 @@ SIGNATURES = {
                        _I32, _I32, _F32, _I32, _P, _P, _P, _P],
     "ls_sparse_attn_gather_only": [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I32, _I32,
                                    _I32, _P, _I32, _I32, _I32, _P, _P],
+    "ls_wait_timeout_probe": [_P, _P, ctypes.c_uint64, _P],
 }
 STRING_FUNCS = ("ls_status_string", "ls_last_error", "ls_version")
 SIZE_FUNCS = {"ls_select_pages_workspace_bytes": [_I64, _I32, _I32],

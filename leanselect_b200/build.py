@@ -21,7 +21,8 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "_lib"
 LIB = LIB_DIR / "libleanselect_b200.so"
-SOURCES = ["prep.cu", "score_select.cu", "sparse_attn.cu", "capi.cu", "backbone.cu", "noalloc.cu"]
+SOURCES = ["prep.cu", "score_select.cu", "sparse_attn.cu", "capi.cu", "backbone.cu", "noalloc.cu",
+           "waitprobe.cu"]
 HEADERS = ["common.cuh", "launch.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -582,6 +582,15 @@ int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                           block_size, softmax_scale, causal, out, lse, status, stream, false);
 }
 
+int ls_wait_timeout_probe(int32_t* status, int32_t* done, uint64_t timeout_ns, void* stream) {
+  LS_REQUIRE(status && done, "null status or done");
+  LS_REQUIRE(timeout_ns >= 1000 && timeout_ns <= LS_WAIT_TIMEOUT_NS,
+             "timeout_ns must lie in [1 us, 2 s]");
+  const cudaError_t err = launch_wait_probe(status, done, timeout_ns,
+                                            static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? LS_OK : cuda_fail(err, "wait probe launch");
+}
+
 int ls_sparse_attn_gather_only(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                                const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
                                int32_t batch, int32_t max_seqlen_q, int32_t max_seqlen_k,

@@ -87,10 +87,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for phase `parity` of `bar` to complete.  Returns false (and records
-// LS_DEVERR_TIMEOUT) if it has not completed after LS_WAIT_TIMEOUT_NS, or if
-// another thread of the CTA already gave up (`abort_flag` set).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status,
-                                          volatile int* abort_flag) {
+// LS_DEVERR_TIMEOUT) if it has not completed after `timeout_ns` of wall
+// time, or if another thread of the CTA already gave up (`abort_flag` set).
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int32_t* status,
+                                              volatile int* abort_flag, uint64_t timeout_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer();
   uint32_t spins = 0;
@@ -98,13 +98,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 63u) == 0) {
       if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer() - start > LS_WAIT_TIMEOUT_NS) {
+      if (globaltimer() - start > timeout_ns) {
         report(status, LS_DEVERR_TIMEOUT);
         if (abort_flag != nullptr) *abort_flag = 1;
         return false;
       }
     }
   }
+}
+
+// mbar_wait_for with the library's limit, LS_WAIT_TIMEOUT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status,
+                                          volatile int* abort_flag) {
+  return mbar_wait_for(bar, parity, status, abort_flag, LS_WAIT_TIMEOUT_NS);
 }
 
 // ---------------------------------------------------------------------------

@@ -110,6 +110,10 @@ int check_select_args(const uint16_t* q, const uint16_t* wq_t, const uint16_t* k
                       int32_t init_blocks, int32_t local_blocks, int32_t block_size,
                       int32_t kernel_stride, const int32_t* topk_idx);
 
+// The bounded-wait test hook (waitprobe.cu).
+cudaError_t launch_wait_probe(int32_t* status, int32_t* done, uint64_t timeout_ns,
+                              cudaStream_t stream);
+
 // Records `message` as the calling thread's ls_last_error() text; returns `code`.
 int set_host_error(int code, const char* message);
 

@@ -360,6 +360,10 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
     sm->l_part[warp][r1] = l1;
   }
   asm volatile("bar.sync 1, 128;" ::: "memory");
+  // A wait that gave up leaves the row unwritten: copies the producer issued
+  // may still be landing in the stage memory the merge below would reuse.
+  // Every consumer warp has either set or seen the flag before the barrier.
+  if (*abort_flag) return;
   float mt0 = -INFINITY, mt1 = -INFINITY;
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
@@ -426,7 +430,6 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
       }
     }
   }
-  (void)ok;
 }
 
 size_t attn_smem_bytes() { return 1024 + kStages * kStageBytes + 16 * 256 + sizeof(AttnSmem); }

@@ -78,6 +78,64 @@ def lpt_shards(lengths: Sequence[int], world: int) -> list[list[int]]:
     return [sorted(s) for s in shards]
 
 
+class RankFailure(RuntimeError):
+    """A rank did not reach a step: it died, left, or stalled past the limit."""
+
+    def __init__(self, step: int, missing: Sequence[int]):
+        super().__init__(f"ranks {list(missing)} did not reach step {step}")
+        self.step = step
+        self.missing = list(missing)
+
+
+class StepPresence:
+    """Host-side presence check between prefill steps.
+
+    Before each step every rank posts ``step/rank`` to the process group's
+    key-value store and waits, up to ``timeout_s``, for all ranks' posts of
+    that step.  A rank that died, left between steps or stalls past the limit
+    makes the others raise :class:`RankFailure` naming it, before they launch
+    a kernel or a collective of the step, so no NCCL collective is left
+    waiting for a peer that will never come.  This plays the role of the
+    reference trainer's per-step presence all-reduce and error broadcast
+    (train.py:270-275, 140), on the store instead of the data path.
+    """
+
+    def __init__(self, group=None, timeout_s: float = 60.0, store=None, prefix: str = "leanselect"):
+        from datetime import timedelta
+
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if store is None:
+            store = dist.distributed_c10d._get_default_store()
+        self.store = store
+        self.timeout = timedelta(seconds=float(timeout_s))
+        self.prefix = prefix
+        self.step = 0
+
+    def _key(self, step: int, rank: int) -> str:
+        return f"{self.prefix}/step{step}/rank{rank}"
+
+    def arrive(self) -> int:
+        """Post this rank's presence for the next step and wait for every rank's."""
+        step = self.step
+        self.step += 1
+        self.store.set(self._key(step, self.rank), "1")
+        keys = [self._key(step, r) for r in range(self.world)]
+        try:
+            self.store.wait(keys, self.timeout)
+        except Exception as exc:  # the store raises its own timeout / connection errors
+            missing = []
+            for r, key in enumerate(keys):
+                try:
+                    present = self.store.check([key])
+                except Exception:
+                    present = False
+                if not present:
+                    missing.append(r)
+            raise RankFailure(step, missing or list(range(self.world))) from exc
+        return step
+
+
 _CU_CACHE: dict[tuple, torch.Tensor] = {}
 
 
@@ -226,13 +284,17 @@ class DataParallelRunner:
     """
 
     def __init__(self, shape: MiniCPMShape, device: torch.device | str, seed: int = 0,
-                 group=None):
+                 group=None, presence_timeout_s: float | None = 300.0):
         self.device = torch.device(device)
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.model = PrefillModel(shape, self.device, seed=seed)
+        self.presence = (StepPresence(group, presence_timeout_s)
+                         if self.world > 1 and presence_timeout_s else None)
 
     def prefill_device(self, ids: torch.Tensor, lengths: Sequence[int]):
+        if self.presence is not None:
+            self.presence.arrive()
         lengths = [int(n) for n in lengths]
         mine = lpt_shards(lengths, self.world)[self.rank]
         if not mine:
@@ -252,7 +314,7 @@ class SequenceParallelRunner:
     """One sequence prefilled by all ranks of the default process group."""
 
     def __init__(self, shape: MiniCPMShape, device: torch.device | str, seed: int = 0,
-                 group=None):
+                 group=None, presence_timeout_s: float | None = 300.0):
         self.device = torch.device(device)
         self.group = group
         self.world = dist.get_world_size(group)
@@ -260,6 +322,8 @@ class SequenceParallelRunner:
         # Same seed on every rank: identical random weights everywhere.
         self.model = PrefillModel(shape, self.device, seed=seed)
         self._cu_cache: dict[tuple, torch.Tensor] = {}
+        # Every rank checks that all ranks reached the step before launching it.
+        self.presence = StepPresence(group, presence_timeout_s) if presence_timeout_s else None
 
     def _cu(self, *values: int) -> torch.Tensor:
         key = tuple(values)
@@ -274,6 +338,8 @@ class SequenceParallelRunner:
         """``ids`` holds the whole sequence on every rank; rank 0 returns ``[1, vocab]`` logits."""
         if len(lengths) != 1:
             raise ValueError("sequence-parallel prefill takes one sequence")
+        if self.presence is not None:
+            self.presence.arrive()
         m, s = self.model, self.model.shape
         n = int(lengths[0])
         chunks = zigzag_chunks(n, self.world, self.rank)

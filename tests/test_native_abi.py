@@ -98,6 +98,15 @@ def test_noalloc_checks_arguments_before_its_scratch_limit():
     assert b"scratch" in lib.ls_last_error()
 
 
+def test_wait_probe_validates_on_host():
+    lib = _native.load()
+    fake = ctypes.c_void_p(1 << 20)
+    assert lib.ls_wait_timeout_probe(None, fake, 1000000, None) == _native.LS_ERR_INVALID_ARGUMENT
+    assert lib.ls_wait_timeout_probe(fake, fake, 10, None) == _native.LS_ERR_INVALID_ARGUMENT
+    assert lib.ls_wait_timeout_probe(fake, fake, 3 * 10 ** 9, None) == _native.LS_ERR_INVALID_ARGUMENT
+    assert b"timeout_ns" in lib.ls_last_error()
+
+
 def test_misaligned_pointer_is_reported():
     lib = _native.load()
     fake = ctypes.c_void_p(1 << 20)
