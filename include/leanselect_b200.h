@@ -218,6 +218,43 @@ int ls_select_pages_noalloc(const uint16_t* q, const uint16_t* wq_t, const uint1
                             int32_t* topk_idx, int32_t* status, void* stream);
 
 /*
+ * ls_compress_keys_f32 -- ls_compress_keys for fp32 keys: CompressK.forward
+ * on fp32 tensors (leanselect/models/minicpm.py:1169-1185), whose output
+ * stays fp32.  k [total_k, G, D] fp32 -> k_compressed [total_c, G, D] fp32.
+ * Each window is summed as kernel_size/kernel_stride runs of kernel_stride
+ * keys (in order), the run sums added and the total scaled by
+ * 1/kernel_size.  G*D must be a multiple of 4.
+ */
+int ls_compress_keys_f32(const float* k, const int32_t* cu_seqlens_k, int32_t batch,
+                         int64_t total_k, int32_t num_kv_heads, int32_t head_dim,
+                         int32_t kernel_size, int32_t kernel_stride, float* k_compressed,
+                         int32_t* cu_seqlens_c, int64_t total_c, int32_t* status, void* stream);
+
+/*
+ * ls_select_pages_f32 -- ls_select_pages for fp32 inputs: the reference's
+ * selection run on fp32 tensors (benchmark config 0), where the fused
+ * weights, projections and scores are fp32 einsums (selector.py:144-214)
+ * and the masking / top-k block is that of minicpm.py:3093-3141.  q
+ * [total_q, H, D] fp32, q_fused [H, D, F] and kv_fused [G, D, F] fp32 (the
+ * reference layout of ls_fold_weights), kc [total_c, G, D] fp32.  Output
+ * and conventions as ls_select_pages (ascending pages, ties to the lower
+ * page, -1 padding).  SIMT fp32 kernels; `workspace` (256-byte aligned)
+ * holds ls_select_pages_f32_workspace_bytes(...) bytes: Qs and Ks fp32 and
+ * one fp32 score per (group, row, page).  Requires D == F == 128,
+ * block_size == 64, kernel_stride == 16, take <= LS_MAX_TOPK.
+ */
+size_t ls_select_pages_f32_workspace_bytes(int64_t total_q, int64_t total_c, int32_t num_kv_heads,
+                                           int32_t max_seqlen_q);
+int ls_select_pages_f32(const float* q, const float* q_fused, const float* kc,
+                        const float* kv_fused, const int32_t* cu_seqlens_q,
+                        const int32_t* cu_seqlens_c, int32_t batch, int32_t max_seqlen_q,
+                        int64_t total_q, int64_t total_c, int32_t num_heads, int32_t num_kv_heads,
+                        int32_t head_dim, int32_t width, int32_t take, int32_t init_blocks,
+                        int32_t local_blocks, int32_t block_size, int32_t kernel_stride,
+                        int32_t* topk_idx, void* workspace, size_t workspace_bytes,
+                        int32_t* status, void* stream);
+
+/*
  * ls_uniform_select_pages -- replaces uniform_prefill_topk_idx
  * (leanselect/ops/uniform.py:185-320), the uniform-method selection that
  * MiniCPMInfLLMv2Attention._lightweight_compressed_attention dispatches to

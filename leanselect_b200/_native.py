@@ -45,6 +45,9 @@ SIGNATURES = {
                         _I32, _I32, _I32, _I32, _P, _P, _SZ, _P, _P],
     "ls_select_pages_noalloc": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32,
                                 _I32, _I32, _I32, _I32, _I32, _I32, _P, _P, _P],
+    "ls_compress_keys_f32": [_P, _P, _I32, _I64, _I32, _I32, _I32, _I32, _P, _P, _I64, _P, _P],
+    "ls_select_pages_f32": [_P, _P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32,
+                            _I32, _I32, _I32, _I32, _I32, _P, _P, _SZ, _P, _P],
     "ls_uniform_select_pages": [_P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32,
                                 _I32, _I32, _I32, _I32, _F32, _P, _P, _SZ, _P, _P],
     "ls_select_pages_chunk": [_P, _P, _P, _I64, _I32, _I32, _I64, _I32, _I32, _I32, _I32, _I32,
@@ -60,6 +63,7 @@ SIGNATURES = {
 }
 STRING_FUNCS = ("ls_status_string", "ls_last_error", "ls_version")
 SIZE_FUNCS = {"ls_select_pages_workspace_bytes": [_I64, _I32, _I32],
+              "ls_select_pages_f32_workspace_bytes": [_I64, _I64, _I32, _I32],
               "ls_uniform_select_workspace_bytes": [_I64, _I64, _I32, _I32, _I32]}
 
 _lock = threading.Lock()

@@ -33,9 +33,10 @@ class CompressK(nn.Module):
         self.kernel_stride = kernel_stride
 
     def forward(self, k: torch.Tensor, cu_seqlens: torch.Tensor, lengths=None):
+        """bf16 keys compress in bf16, fp32 keys in fp32; other dtypes go through bf16."""
         kc, cu_c = ops.compress_keys(k, cu_seqlens, kernel_size=self.kernel_size,
                                      kernel_stride=self.kernel_stride, lengths=lengths)
-        if k.dtype != torch.bfloat16:
+        if kc.dtype != k.dtype:
             kc = kc.to(k.dtype)
         return kc, cu_c
 
@@ -83,6 +84,14 @@ def lightweight_compressed_attention(module, q_unpad: torch.Tensor, k_compressed
     block = int(module.block_size)
     max_pages = max(((n + block - 1) // block for n in lengths), default=0)
     take = min(int(module.topk), max_pages)
+    if q_unpad.dtype == torch.float32:
+        # fp32 inputs are selected in fp32, as the reference's fp32 einsums do.
+        q_fused, kv_fused = selector.fused_weights()
+        return ops.select_pages_f32(q_unpad, q_fused, k_compressed, kv_fused, cu_seqlens_q,
+                                    cu_seqlens_k, int(max(lengths, default=0)), take=take,
+                                    init_blocks=int(module.init_blocks),
+                                    local_blocks=int(module.local_blocks), block_size=block,
+                                    kernel_stride=int(module.kernel_stride))
     weights = selector.kernel_weights()
     ks = ops.project_atom_keys(k_compressed, weights.wk_t)
     return ops.select_pages(q_unpad, weights, ks, cu_seqlens_q, cu_seqlens_k,

@@ -22,8 +22,8 @@ CSRC = PKG / "csrc"
 LIB_DIR = PKG / "_lib"
 LIB = LIB_DIR / "libleanselect_b200.so"
 SOURCES = ["prep.cu", "score_select.cu", "sparse_attn.cu", "capi.cu", "backbone.cu", "noalloc.cu",
-           "waitprobe.cu"]
-HEADERS = ["common.cuh", "launch.h"]
+           "waitprobe.cu", "select_f32.cu"]
+HEADERS = ["common.cuh", "launch.h", "topk_rows.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",

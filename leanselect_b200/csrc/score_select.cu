@@ -37,6 +37,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "topk_rows.cuh"
 
 namespace ls {
 namespace {
@@ -561,126 +562,6 @@ struct KeptKeys {         // entry j of the warp's kept buffer
   __device__ __forceinline__ uint32_t operator()(int j) const { return k[j] >> 16; }
 };
 
-// Exclusive prefix sum over the warp; returns it and sets `total`.
-__device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
-  int incl = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int t = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += t;
-  }
-  total = __shfl_sync(0xffffffffu, incl, 31);
-  return incl - v;
-}
-
-// Exact threshold of the `need` largest nonzero 16-bit keys among
-// keys(0 .. count-1), need >= 1.  A histogram over the keys' own range:
-// 256 bins of width 2^shift from the smallest key, so one pass is exact
-// when the keys span fewer than 256 values and a second pass over the bin
-// that holds the threshold finishes otherwise.  Returns the threshold key;
-// `need` becomes the number of keys equal to it that belong to the
-// selection (the lowest indices win).
-template <class Keys>
-__device__ uint32_t radix_threshold16(const Keys& keys, int count, int& need, uint32_t* hist,
-                                      int lane) {
-  uint32_t kmin = 0xFFFFu, kmax = 0u;
-  for (int i = lane; i < count; i += 32) {
-    const uint32_t key = keys(i);
-    if (key != 0u) {
-      kmin = min(kmin, key);
-      kmax = max(kmax, key);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
-    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
-  }
-  const uint32_t range = kmax - kmin;
-  int shift = range > 255u ? (32 - __clz(range)) - 8 : 0;  // (range >> shift) < 256
-  uint32_t lo = kmin;        // keys of the current pass: [lo, lo + (256 << shift))
-  uint32_t width = 256u << shift;
-#pragma unroll 1
-  while (true) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) hist[lane + 32 * j] = 0;
-    __syncwarp();
-    for (int i = lane; i < count; i += 32) {
-      const uint32_t key = keys(i);
-      if (key != 0u && key >= lo && key - lo < width) atomicAdd(&hist[(key - lo) >> shift], 1u);
-    }
-    __syncwarp();
-    // Lane l owns bins 255-8l .. 248-8l (descending).
-    uint32_t c[8];
-    uint32_t lane_sum = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      c[j] = hist[255 - 8 * lane - j];
-      lane_sum += c[j];
-    }
-    uint32_t incl = lane_sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
-    }
-    const uint32_t excl = incl - lane_sum;
-    const bool here = excl < static_cast<uint32_t>(need) && incl >= static_cast<uint32_t>(need);
-    const uint32_t owner_mask = __ballot_sync(0xffffffffu, here);
-    const int owner = __ffs(owner_mask) - 1;
-    int bin = 0;
-    uint32_t above = 0;
-    if (here) {
-      uint32_t cum = excl;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (cum + c[j] >= static_cast<uint32_t>(need)) {
-          bin = 255 - 8 * lane - j;
-          above = cum;
-          break;
-        }
-        cum += c[j];
-      }
-    }
-    bin = __shfl_sync(0xffffffffu, bin, owner);
-    above = __shfl_sync(0xffffffffu, above, owner);
-    need -= static_cast<int>(above);
-    __syncwarp();
-    lo += static_cast<uint32_t>(bin) << shift;
-    if (shift == 0) return lo;
-    width = 1u << shift;   // the bin's keys, one per bin in the next pass
-    shift = 0;
-  }
-}
-
-// Writes, in index order, the entries among keys(0 .. count-1) above `thr`
-// plus the first `ties` equal to it, as page numbers `index(j) + base`;
-// candidate `skip` is selected but not written.  Returns the next output
-// position.
-template <class Keys, class Index>
-__device__ int emit_threshold(const Keys& keys, const Index& index, int count, uint32_t thr,
-                              int ties, int skip, int base, int32_t* out, int k_out, int lane) {
-  int ties_seen = 0;
-  for (int b0 = 0; b0 < count; b0 += 32) {
-    const int j = b0 + lane;
-    const uint32_t key = j < count ? keys(j) : 0u;
-    const bool tie = key == thr && key != 0u;
-    const uint32_t tie_mask = __ballot_sync(0xffffffffu, tie);
-    const int tie_rank = ties_seen + __popc(tie_mask & ((1u << lane) - 1));
-    ties_seen += __popc(tie_mask);
-    bool take = key > thr || (tie && tie_rank < ties);
-    const int i = j < count ? index(j) : -1;
-    if (i == skip) take = false;  // the slot page qp+1 won stays empty
-    const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
-    if (take) out[k_out + __popc(take_mask & ((1u << lane) - 1))] = base + i;
-    k_out += __popc(take_mask);
-  }
-  return k_out;
-}
-
-struct Identity {
-  __device__ __forceinline__ int operator()(int j) const { return j; }
-};
 struct KeptIndex {
   const uint32_t* k;
   __device__ __forceinline__ int operator()(int j) const { return static_cast<int>(k[j] & 0xFFFFu); }
@@ -867,7 +748,7 @@ __device__ int select_row(const Src& src, const GlobalChunks& row, int off, int 
   int need = cap;
   if (kept >= cap && kept <= kKeptCap) {
     const KeptKeys kk{ws->kept};
-    const uint32_t thr = radix_threshold16(kk, kept, need, ws->hist, lane);
+    const uint32_t thr = radix_threshold(kk, kept, need, ws->hist, lane);
     return emit_threshold(kk, KeptIndex{ws->kept}, kept, thr, need, skip, n_init, out, k_out, lane);
   }
   // ---- exact radix over the whole row (the estimate kept too few or too many).
@@ -877,7 +758,7 @@ __device__ int select_row(const Src& src, const GlobalChunks& row, int off, int 
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) finite += __shfl_xor_sync(0xffffffffu, finite, o);
   if (finite <= cap) return k_out + compact_ge(row, off, m_out, finite2, write_out, lane);
-  const uint32_t thr = radix_threshold16(row_keys, m, need, ws->hist, lane);
+  const uint32_t thr = radix_threshold(row_keys, m, need, ws->hist, lane);
   return emit_threshold(row_keys, Identity{}, m, thr, need, skip, n_init, out, k_out, lane);
 }
 
@@ -886,7 +767,8 @@ struct RowPlan {
   bool valid;           // a row to process
   bool empty;           // the row stays all -1 (bad seqlens, or no atoms outside uniform)
   int32_t* out;
-  const uint4* row4;    // the candidates' 16-byte chunks in the workspace
+  int64_t ws_row;       // element offset of the row in the workspace
+  const uint4* row4;    // the candidates' 16-byte chunks in the workspace (bf16 rows)
   int off, nch;         // candidate i is element off + i of nch chunks
   int m_all, cap, future, n_init, take_b, local0, n_local;
   bool staged;          // copied into the warp's shared memory
@@ -897,56 +779,13 @@ __device__ __forceinline__ RowPlan plan_row(const ScoreArgs& args, uint32_t r, u
   RowPlan p{};
   p.valid = r < rows_total;
   if (!p.valid) return p;
-  const int64_t q_row = r % total_q;
-  p.out = args.topk_idx + static_cast<int64_t>(r) * args.take;
-  int b = 0, n;
-  int64_t q0 = 0;
-  if (args.cu_q) {
-    b = find_sequence(args.cu_q, args.batch, q_row);
-    q0 = __ldg(args.cu_q + b);
-    n = static_cast<int>(__ldg(args.cu_q + b + 1) - q0);
-    if (n > args.max_seqlen_q) {  // reported by score_kernel; the row stays empty
-      p.empty = true;
-      return p;
-    }
-  } else {
-    n = args.max_seqlen_q;
-  }
-  const int atoms = args.cu_c ? static_cast<int>(__ldg(args.cu_c + b + 1) - __ldg(args.cu_c + b))
-                              : static_cast<int>(args.total_c);
-  const int pos = args.pos_offset + static_cast<int>(q_row - q0);
-  const int pages = ((args.seq_len > 0 ? args.seq_len : n) + 63) / 64;
-  const int qp = pos / 64;
-  p.take_b = min(args.take, pages);
-  p.n_init = min(args.init_blocks, qp + 1);             // sink pages 0 .. n_init-1
-  const int lo = max(0, qp - args.local_blocks);         // local pages lo .. qp
-  p.local0 = max(lo, p.n_init);
-  p.n_local = qp - p.local0 + 1;                         // local pages that are not sinks
-  int m = max(0, lo - p.n_init);                         // candidates n_init .. lo-1
-  int slots = p.take_b - (p.n_init + p.n_local);
-  // Uniform method: page qp+1 is scored too (its first window atom may be
-  // visible) and competes as candidate m, or as a forced sink; either way
-  // a slot it wins stays -1 (uniform.py:100-106).  Rows of sequences
-  // without atoms keep their forced pages (head_mix.py:150-170).
-  p.future = -1;
-  if (args.uniform) {
-    if (atoms <= 0) m = 0;
-    slots -= max(0, min(args.init_blocks, pages) - (qp + 1));  // future sinks
-    if (atoms > 0 && qp + 1 < pages && qp + 1 >= args.init_blocks) p.future = m;
-  } else if (atoms <= 0) {
-    // The reference leaves rows of sequences without atoms at -1 (minicpm.py:3115-3116).
-    p.empty = true;
-    return p;
-  }
-  p.m_all = m + (p.future >= 0 ? 1 : 0);
-  p.cap = max(0, min(slots, p.m_all));
-  // Candidate i is page n_init + i; candidate m (page qp+1) was stored by
-  // the score kernel in slot n_init + m, the first non-sink local page.
+  row_geometry(args, r, total_q, &p.out, &p.ws_row, &p.empty, &p.m_all, &p.cap, &p.future,
+               &p.n_init, &p.take_b, &p.local0, &p.n_local);
+  if (p.empty) return p;
   // Chunks start at the 8-page boundary below the first candidate (rows are
   // 16-byte aligned).
   p.off = p.n_init & 7;
-  p.row4 = reinterpret_cast<const uint4*>(args.workspace + static_cast<int64_t>(r) * args.max_pages) +
-           (p.n_init >> 3);
+  p.row4 = reinterpret_cast<const uint4*>(args.workspace + p.ws_row) + (p.n_init >> 3);
   p.nch = (p.off + p.m_all + 7) >> 3;
   p.staged = p.cap > 0 && p.nch <= kRowChunks;
   return p;

@@ -196,11 +196,21 @@ def compress_keys(k: torch.Tensor, cu_seqlens_k: torch.Tensor, *, kernel_size: i
     dev = _require_cuda(k, cu_seqlens_k)
     if k.ndim != 3:
         raise ValueError("k must be [total_k, num_kv_heads, head_dim]")
-    kb = _bf16(k)
     cu = _i32(cu_seqlens_k)
     if total_c is None:
         lens = list(lengths) if lengths is not None else host_lengths(cu)
         total_c = sum(atom_count(n, kernel_size, kernel_stride) for n in lens)
+    if k.dtype == torch.float32:
+        # fp32 keys stay fp32, as CompressK keeps the input dtype.
+        kf = k.contiguous()
+        kc = torch.empty(total_c, k.shape[1], k.shape[2], dtype=torch.float32, device=dev)
+        cu_c = torch.empty_like(cu)
+        _call(dev, "ls_compress_keys_f32", kf.data_ptr(), cu.data_ptr(), cu.numel() - 1,
+              kf.shape[0], k.shape[1], k.shape[2], kernel_size, kernel_stride,
+              _ptr(kc) if total_c else None, cu_c.data_ptr(), total_c,
+              status_word(dev).data_ptr(), _stream(dev))
+        return kc, cu_c
+    kb = _bf16(k)
     kc = torch.empty(total_c, k.shape[1], k.shape[2], dtype=torch.bfloat16, device=dev)
     cu_c = torch.empty_like(cu)
     _call(dev, "ls_compress_keys", kb.data_ptr(), cu.data_ptr(), cu.numel() - 1, kb.shape[0],
@@ -312,6 +322,39 @@ def select_pages(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
                weights.head_dim, weights.width, int(take), int(init_blocks), int(local_blocks),
                block_size, kernel_stride, idx.data_ptr(), ws.data_ptr(), ws.numel(),
                status_word(dev).data_ptr(), _stream(dev))
+    return idx
+
+
+def select_pages_f32(q: torch.Tensor, q_fused: torch.Tensor, kc: torch.Tensor,
+                     kv_fused: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                     cu_seqlens_c: torch.Tensor, max_seqlen_q: int, *, take: int,
+                     init_blocks: int = 1, local_blocks: int = 2, block_size: int = 64,
+                     kernel_stride: int = 16) -> torch.Tensor:
+    """Selection of fp32 inputs in fp32 (the reference's fp32 einsums): ``[G, total_q, take]``.
+
+    ``q_fused [H, D, F]`` / ``kv_fused [G, D, F]`` are the fp32 folded
+    weights (``fused_weights()``), ``kc [total_c, G, D]`` the fp32 atoms.
+    """
+    dev = _require_cuda(q, q_fused, kc, kv_fused, cu_seqlens_q, cu_seqlens_c)
+    qf = q.float().contiguous()
+    kcf = kc.float().contiguous()
+    wq, wk = q_fused.float().contiguous(), kv_fused.float().contiguous()
+    total_q, H, D = qf.shape
+    total_c, G = kcf.shape[0], kcf.shape[1]
+    if take > LS_MAX_TOPK:
+        raise ValueError(f"take={take} exceeds LS_MAX_TOPK={LS_MAX_TOPK}")
+    idx = torch.empty(G, total_q, take, dtype=torch.int32, device=dev)
+    if take == 0 or total_q == 0:
+        return idx
+    cu_q, cu_c = _i32(cu_seqlens_q), _i32(cu_seqlens_c)
+    nbytes = _native.load().ls_select_pages_f32_workspace_bytes(total_q, total_c, G,
+                                                                int(max_seqlen_q))
+    ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=dev)
+    _call(dev, "ls_select_pages_f32", qf.data_ptr(), wq.data_ptr(),
+          kcf.data_ptr() if total_c else None, wk.data_ptr(), cu_q.data_ptr(), cu_c.data_ptr(),
+          cu_q.numel() - 1, int(max_seqlen_q), total_q, total_c, H, G, D, wq.shape[-1], int(take),
+          int(init_blocks), int(local_blocks), block_size, kernel_stride, idx.data_ptr(),
+          ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(), _stream(dev))
     return idx
 
 

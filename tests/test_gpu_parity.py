@@ -846,3 +846,84 @@ def test_custom_op_traces_under_torch_compile():
     got_out, got_lse = compiled(q, k, v, cu, idx)
     want_out, want_lse = layer(q, k, v, cu, idx)
     assert torch.equal(got_out, want_out) and torch.equal(got_lse, want_lse)
+
+
+# ---------------------------------------------------------------------------
+# fp32 inputs (benchmark config 0): selected in fp32, as the reference does
+# ---------------------------------------------------------------------------
+
+def test_config0_fp32_selection_matches_reference_fixture():
+    """benchmark config 0 (N=8192, fp32, T=35 = 32 + sink + 2 local): GPU
+    compression bit-exact with the oracle's fp32 order; GPU selection against
+    the reference's own topk_idx rows (tests/golden/config0.npz) and against
+    the fp32 oracle on every row, differences only at fp32 ties (1e-3)."""
+    import pathlib
+    g = np.load(pathlib.Path(__file__).parent / "golden" / "config0.npz")
+    inp = ora.synthetic_layer([8192], seed=int(g["seed"]))
+    cu = cu_dev(inp.cu_seqlens)
+    k32 = torch.from_numpy(inp.k).to(DEV)
+    kc, cu_c = lsb.CompressK(2, 128, 32, 16)(k32, cu)
+    assert kc.dtype == torch.float32
+    ekc, ecu = ora.compress_keys(inp.k, inp.cu_seqlens)
+    np.testing.assert_array_equal(kc.cpu().numpy(), ekc)
+    np.testing.assert_allclose(ekc[::50], g["kc_rows"], rtol=1e-5, atol=1e-6)
+    sel = selector_for(inp.params)
+    from leanselect_b200.attention import _LayerView
+    view = _LayerView(lsb.LayerConfig(topk=35), sel)
+    got = lsb.lightweight_compressed_attention(view, torch.from_numpy(inp.q).to(DEV), kc, cu,
+                                               cu_c, 8192).cpu().numpy()
+    want = ora.lightweight_compressed_attention(inp.q, ekc, inp.cu_seqlens, ecu, inp.params,
+                                                topk=35)
+    bad = ora.selection_mismatches(got, want, rel_tol=1e-3)
+    assert not bad, bad[:5]
+    rows = g["rows"]
+    ref = ora.Selection(g["idx_rows"].astype(np.int32), want.boundary[:, rows],
+                        [(0, want.page_scores[0][1][:, rows])])
+    bad = ora.selection_mismatches(got[:, rows], ref, rel_tol=1e-3)
+    assert not bad, bad[:5]
+    assert ops.check_status(DEV) == 0
+
+
+def test_fp32_selection_packed_batch_matches_oracle():
+    lens = [3000, 20, 1500, 64, 2100]
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=3, seed=77)
+    cu = cu_dev(inp.cu_seqlens)
+    kc, cu_c = ops.compress_keys(torch.from_numpy(inp.k).to(DEV), cu)
+    ekc, ecu = ora.compress_keys(inp.k, inp.cu_seqlens)
+    np.testing.assert_array_equal(kc.cpu().numpy(), ekc)
+    np.testing.assert_array_equal(cu_c.cpu().numpy(), ecu)
+    for topk, init, local in ((12, 1, 2), (40, 2, 4)):
+        sel = selector_for(inp.params)
+        from leanselect_b200.attention import _LayerView
+        view = _LayerView(lsb.LayerConfig(topk=topk, init_blocks=init, local_blocks=local), sel)
+        got = lsb.lightweight_compressed_attention(view, torch.from_numpy(inp.q).to(DEV), kc, cu,
+                                                   cu_c, max(lens)).cpu().numpy()
+        want = ora.lightweight_compressed_attention(inp.q, ekc, inp.cu_seqlens, ecu, inp.params,
+                                                    topk=topk, init_blocks=init,
+                                                    local_blocks=local)
+        assert got.shape == want.topk_idx.shape
+        bad = ora.selection_mismatches(got, want, rel_tol=1e-3)
+        assert not bad, bad[:5]
+    assert ops.check_status(DEV) == 0
+
+
+def test_config0_attention_against_fp32_oracle():
+    """Stage 2 of config 0: the InfLLM-v2 kernel the reference calls takes
+    fp16/bf16 only, so fp32 q/k/v are attended in bf16 (fp32 accumulation);
+    north_star's tolerance is stated against the fp32 reference."""
+    inp = ora.synthetic_layer([8192], seed=0)
+    cu = cu_dev(inp.cu_seqlens)
+    ekc, ecu = ora.compress_keys(inp.k, inp.cu_seqlens)
+    rows = np.unique(np.concatenate([np.arange(0, 200, 7), np.arange(8192 - 100, 8192),
+                                     np.random.default_rng(4).integers(0, 8192, 120)]))
+    sel = ora.select_rows(inp.q, ekc, inp.params, rows, take=35, policy="fp32")
+    idx = np.full((2, 8192, 35), -1, dtype=np.int32)
+    idx[:, rows] = sel.topk_idx
+    out = lsb.infllmv2_attn_varlen_func(
+        torch.from_numpy(inp.q).to(DEV), torch.from_numpy(inp.k).to(DEV),
+        torch.from_numpy(inp.v).to(DEV), cu, cu, 8192, 8192, causal=True,
+        topk_idx=to_dev(idx, torch.int32))
+    assert out.dtype == torch.float32
+    ref = ora.attention_for_queries(inp.q[rows], rows, inp.k, inp.v, sel.topk_idx)
+    _attn_check(out[torch.from_numpy(rows).to(DEV)], None, ref, None)
