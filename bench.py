@@ -123,12 +123,15 @@ class ClockSampler:
 class CpuHotPath:
     """The oracle restatement of one layer's hot path on the host cores.
 
-    Compression runs on the whole sequence; selection and attention run for
-    ``rows`` query rows drawn from the last quarter of the sequence (where
-    every row has its full page budget) and are scaled to all rows.  Input
-    generation happens once, outside the timed steps.  Throughput is the hot
-    path's tokens/s for ``layers`` layers (the dense backbone GEMMs are not
-    included, which favours the CPU).
+    Per-layer work runs once on the whole layer: compression of all keys,
+    the selector's weight folding and the projection of every atom.  Per-row
+    work -- the query projection, the row's atom scores, pooling, masking and
+    top-k, and the row's sparse attention -- runs for ``rows`` query rows
+    drawn from the last quarter of the sequence (where every row has its full
+    page budget) and is scaled to all rows.  Input generation happens once,
+    outside the timed steps.  Throughput is the hot path's tokens/s for
+    ``layers`` layers (the dense backbone GEMMs are not included, which
+    favours the CPU).
     """
 
     def __init__(self, seq_len: int, layers: int, rows: int, seed: int):
@@ -149,8 +152,12 @@ class CpuHotPath:
         ora, n = self.ora, self.seq_len
         t0 = time.perf_counter()
         kc, _ = ora.compress_keys(self.k, self.cu, policy="bf16")
+        q_fused, kv_fused = ora.fold_weights(self.params, "bf16")
+        ks = ora.project_atom_keys(kc, kv_fused, "bf16")
         t1 = time.perf_counter()
-        sel = ora.select_for_queries(self.q, self.sample, n, kc, self.params, take=67)
+        qs = ora.project_queries(self.q, q_fused, self.params.num_kv_heads, "bf16")
+        pages = ora.pool_atoms_to_pages(ora.atom_scores(qs, ks, "bf16"), n)
+        sel = ora.select_from_scores(pages, self.sample, take=67)
         ora.attention_for_queries(self.q, self.sample, self.k, self.v, sel.topk_idx)
         t2 = time.perf_counter()
         per_layer = (t1 - t0) + (t2 - t1) * n / self.rows
@@ -158,13 +165,14 @@ class CpuHotPath:
         return n / (per_layer * self.layers)
 
     def describe(self, value: float) -> dict:
-        tc, ts = self.last
+        tl, tr = self.last
         return {
             "value": value, "unit": "tokens/s", "cores": self.cores, "kind": "port",
-            "sample": (f"one {self.seq_len}-token layer of the oracle hot path: full compression "
-                       f"({tc:.2f} s) plus selection+attention for {self.rows} query rows "
-                       f"({ts:.2f} s), scaled to {self.seq_len} rows and {self.layers} layers; "
-                       "dense backbone not included"),
+            "sample": (f"one {self.seq_len}-token layer of the oracle hot path: per-layer work "
+                       f"(compression, weight folding, atom projection: {tl:.2f} s) once, plus "
+                       f"per-row work (query projection, scores, top-k, attention) for "
+                       f"{self.rows} query rows ({tr:.2f} s) scaled to {self.seq_len} rows; "
+                       f"x {self.layers} layers; dense backbone not included"),
         }
 
 
@@ -316,6 +324,10 @@ def run_ours(args):
         from datetime import timedelta
         from leanselect_b200.parallel import SequenceParallelRunner
 
+        # NCCL's initialisation log (one line set per rank and channel) shows
+        # how many ranks joined and over which transport.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
         runner = SequenceParallelRunner(shape, dev, seed=args.seed)
     else:

@@ -95,14 +95,34 @@ int ls_compressed_seqlens(const int32_t* cu_seqlens_k, int32_t batch, int32_t ke
  * k [total_k, G, D] bf16 -> k_compressed [total_c, G, D] bf16 and
  * cu_seqlens_c [batch+1].  Atom i of sequence b is the mean of keys
  * [16 i, 16 i + 32) of that sequence (kernel_size/kernel_stride in general,
- * kernel_size a multiple of kernel_stride).  total_c must equal the value
- * implied by cu_seqlens_k (the caller computes it, as the reference does on
- * the host); G*D must be a multiple of 8 and at most 2048.
+ * kernel_size a multiple of kernel_stride), summed in fp32 as runs of 16
+ * keys (of kernel_stride keys when 16 does not divide it), the run sums
+ * added in order, then scaled and rounded to bf16.  total_c must equal the
+ * value implied by cu_seqlens_k (the caller computes it, as the reference
+ * does on the host); G*D must be a multiple of 8 and at most 2048.
  */
 int ls_compress_keys(const uint16_t* k, const int32_t* cu_seqlens_k, int32_t batch,
                      int64_t total_k, int32_t num_kv_heads, int32_t head_dim,
                      int32_t kernel_size, int32_t kernel_stride, uint16_t* k_compressed,
                      int32_t* cu_seqlens_c, int64_t total_c, int32_t* status, void* stream);
+
+/*
+ * ls_compress_keys_dual -- both compressions of a prefill in one pass over
+ * K: the compress_k (kernel 32, stride 16) and compress_k2 (kernel 128,
+ * stride 64) calls of MiniCPMInfLLMv2Attention.get_compress_k
+ * (leanselect/models/minicpm.py:2785-2792).  Outputs equal, bit for bit,
+ * ls_compress_keys with (32, 16) and with (128, 64): every window is summed
+ * as 16-key runs in fp32, the run sums added in order, scaled and rounded to
+ * bf16.  k [total_k, G, D] bf16 -> k_compressed [total_c, G, D] +
+ * cu_seqlens_c, k_compressed2 [total_c2, G, D] + cu_seqlens_c2; the totals
+ * are those cu_seqlens_k implies (the caller computes them, as the
+ * reference does on the host); max_seqlen_k bounds the sequences' lengths.
+ */
+int ls_compress_keys_dual(const uint16_t* k, const int32_t* cu_seqlens_k, int32_t batch,
+                          int32_t max_seqlen_k, int64_t total_k, int32_t num_kv_heads,
+                          int32_t head_dim, uint16_t* k_compressed, int32_t* cu_seqlens_c,
+                          int64_t total_c, uint16_t* k_compressed2, int32_t* cu_seqlens_c2,
+                          int64_t total_c2, int32_t* status, void* stream);
 
 /*
  * ls_project_atom_keys -- replaces LeanSelectSelector.project_atom_keys

@@ -35,6 +35,8 @@ SIGNATURES = {
     "ls_fold_weights": [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P],
     "ls_compressed_seqlens": [_P, _I32, _I32, _I32, _P, _P, _P],
     "ls_compress_keys": [_P, _P, _I32, _I64, _I32, _I32, _I32, _I32, _P, _P, _I64, _P, _P],
+    "ls_compress_keys_dual": [_P, _P, _I32, _I32, _I64, _I32, _I32, _P, _P, _I64, _P, _P, _I64, _P,
+                              _P],
     "ls_project_atom_keys": [_P, _I64, _I32, _I32, _P, _I32, _P, _P],
     "ls_project_queries": [_P, _I64, _I32, _I32, _I32, _P, _I32, _P, _P, _P],
     "ls_score_pages": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _I32,

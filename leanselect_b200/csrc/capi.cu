@@ -141,6 +141,8 @@ int ls_compress_keys(const uint16_t* k, const int32_t* cu_seqlens_k, int32_t bat
   const int runs = kernel_size / kernel_stride;
   if (runs != 1 && runs != 2 && runs != 4)
     return fail(LS_ERR_UNSUPPORTED, "kernel_size/kernel_stride must be 1, 2 or 4");
+  if (kernel_size / compress_run_length(kernel_stride) > 64)
+    return fail(LS_ERR_UNSUPPORTED, "kernel_size must be at most 64 runs of 16 keys");
   const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;
   if (row % 8 != 0 || row > 2048)
     return fail(LS_ERR_UNSUPPORTED, "num_kv_heads*head_dim must be a multiple of 8 and <= 2048");
@@ -155,6 +157,38 @@ int ls_compress_keys(const uint16_t* k, const int32_t* cu_seqlens_k, int32_t bat
   err = launch_compress_keys(k, cu_seqlens_k, cu_seqlens_c, batch, total_k, total_c, num_kv_heads,
                              head_dim, kernel_size, kernel_stride, k_compressed, status, s);
   return err == cudaSuccess ? LS_OK : cuda_fail(err, "compress_keys launch");
+}
+
+int ls_compress_keys_dual(const uint16_t* k, const int32_t* cu_seqlens_k, int32_t batch,
+                          int32_t max_seqlen_k, int64_t total_k, int32_t num_kv_heads,
+                          int32_t head_dim, uint16_t* k_compressed, int32_t* cu_seqlens_c,
+                          int64_t total_c, uint16_t* k_compressed2, int32_t* cu_seqlens_c2,
+                          int64_t total_c2, int32_t* status, void* stream) {
+  LS_REQUIRE(k && cu_seqlens_k && cu_seqlens_c && cu_seqlens_c2, "null argument");
+  LS_REQUIRE(batch >= 1 && batch <= 65535 && total_k >= 0 && total_c >= 0 && total_c2 >= 0 &&
+                 max_seqlen_k >= 0,
+             "bad sizes");
+  LS_REQUIRE(total_c == 0 || k_compressed, "null k_compressed");
+  LS_REQUIRE(total_c2 == 0 || k_compressed2, "null k_compressed2");
+  LS_REQUIRE(num_kv_heads > 0 && head_dim > 0, "bad head geometry");
+  const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;
+  if (row % 8 != 0 || row > 2048)
+    return fail(LS_ERR_UNSUPPORTED, "num_kv_heads*head_dim must be a multiple of 8 and <= 2048");
+  LS_REQUIRE_ALIGNED(k);
+  LS_REQUIRE_ALIGNED(k_compressed);
+  LS_REQUIRE_ALIGNED(k_compressed2);
+  LS_REQUIRE(total_c <= total_k / 16 + batch && total_c2 <= total_k / 64 + batch,
+             "atom totals exceed the possible counts");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t err = launch_compressed_seqlens(cu_seqlens_k, batch, 32, 16, cu_seqlens_c, status, s);
+  if (err == cudaSuccess)
+    err = launch_compressed_seqlens(cu_seqlens_k, batch, 128, 64, cu_seqlens_c2, status, s);
+  const int max_atoms = max_seqlen_k >= 32 ? (max_seqlen_k - 32) / 16 + 1 : 0;
+  if (err == cudaSuccess && total_c > 0)
+    err = launch_compress_keys_dual(k, cu_seqlens_k, cu_seqlens_c, cu_seqlens_c2, batch, max_atoms,
+                                    total_k, num_kv_heads, head_dim, k_compressed, k_compressed2,
+                                    status, s);
+  return err == cudaSuccess ? LS_OK : cuda_fail(err, "compress_keys_dual launch");
 }
 
 int ls_project_atom_keys(const uint16_t* kc, int64_t total_c, int32_t num_kv_heads,

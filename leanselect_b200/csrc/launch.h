@@ -17,10 +17,23 @@ cudaError_t launch_compressed_seqlens(const int32_t* cu_k, int batch, int kernel
                                       int kernel_stride, int32_t* cu_c, int32_t* status,
                                       cudaStream_t stream);
 
+// Keys summed per run when compressing with stride `kernel_stride`: 16 when
+// 16 divides the stride, else the stride (the summation order of the
+// compression kernels and of the oracle).
+inline int compress_run_length(int kernel_stride) {
+  return kernel_stride % 16 == 0 ? 16 : kernel_stride;
+}
+
 cudaError_t launch_compress_keys(const uint16_t* k, const int32_t* cu_k, const int32_t* cu_c,
                                  int batch, int64_t total_k, int64_t total_c, int G, int D,
                                  int kernel_size, int kernel_stride, uint16_t* kc,
                                  int32_t* status, cudaStream_t stream);
+
+// compress_k (32/16) and compress_k2 (128/64) in one pass over K.
+cudaError_t launch_compress_keys_dual(const uint16_t* k, const int32_t* cu_k, const int32_t* cu_c,
+                                      const int32_t* cu_c2, int batch, int max_atoms,
+                                      int64_t total_k, int G, int D, uint16_t* kc, uint16_t* kc2,
+                                      int32_t* status, cudaStream_t stream);
 
 // Score/select kernel family (score_select.cu).
 enum ScoreMode { kModeProject = 0, kModeScore = 1, kModeSelect = 2, kModeAtoms = 3 };

@@ -113,16 +113,16 @@ __global__ void compressed_seqlens_kernel(const int32_t* __restrict__ cu_k, int 
 //
 // One thread per (packed atom, 16-byte vector of 8 channels).  Consecutive
 // threads cover one key row (512 bytes for G*D = 256), so every load is a
-// fully coalesced row.  A thread sums its window as R = kernel_size / stride
-// runs of `stride` tokens (each run sequentially in fp32), adds the run sums
-// in order, scales by 1/kernel_size and rounds to bf16 -- the oracle's order,
-// so results match it bit for bit.  Each key is read by R atoms; the second
-// read of a run hits L2.
+// fully coalesced row.  A thread sums its window as runs of `run_len` keys
+// (16 when 16 divides the stride, each run sequentially in fp32), adds the
+// run sums in order, scales by 1/kernel_size and rounds to bf16 -- the
+// oracle's order, so results match it bit for bit.  Each key is read by
+// several atoms; the later reads of a run hit L2.
 
 __global__ void __launch_bounds__(256) compress_keys_kernel(
     const uint4* __restrict__ k, const int32_t* __restrict__ cu_k, const int32_t* __restrict__ cu_c,
-    int batch, int64_t total_k, int64_t total_c, int vecs_per_row, int runs, int stride,
-    float inv_kernel, uint4* __restrict__ kc, int32_t* status) {
+    int batch, int64_t total_k, int64_t total_c, int vecs_per_row, int runs, int run_len,
+    int stride, float inv_kernel, uint4* __restrict__ kc, int32_t* status) {
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t atom = gid / vecs_per_row;
   const int vec = static_cast<int>(gid % vecs_per_row);
@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(256) compress_keys_kernel(
   const int b = find_sequence(cu_c, batch, atom);
   const int64_t local = atom - __ldg(cu_c + b);
   const int64_t tok0 = __ldg(cu_k + b) + local * stride;
-  if (tok0 + static_cast<int64_t>(runs) * stride > total_k) {
+  if (tok0 + static_cast<int64_t>(runs) * run_len > total_k) {
     report(status, LS_DEVERR_SEQLENS);
     return;
   }
@@ -143,8 +143,8 @@ __global__ void __launch_bounds__(256) compress_keys_kernel(
 #pragma unroll
     for (int c = 0; c < 8; ++c) run[c] = 0.f;
 #pragma unroll 4
-    for (int t = 0; t < stride; ++t) {
-      const uint4 u = __ldg(src + (static_cast<int64_t>(j) * stride + t) * vecs_per_row);
+    for (int t = 0; t < run_len; ++t) {
+      const uint4 u = __ldg(src + (static_cast<int64_t>(j) * run_len + t) * vecs_per_row);
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -238,6 +238,104 @@ cudaError_t launch_compressed_seqlens(const int32_t* cu_k, int batch, int kernel
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Both compressions of a prefill in one pass over K (get_compress_k,
+// minicpm.py:2774-2810: compress_k with kernel 32 / stride 16 and compress_k2
+// with kernel 128 / stride 64)
+// ---------------------------------------------------------------------------
+//
+// One thread per (sequence, 64-key block b, 16-byte vector).  It sums the
+// 16-key runs 4b .. 4b+7 of its vector (each sequentially in fp32) and
+// writes the 32/16 atoms 4b .. 4b+3 (runs a and a+1 added) and the 128/64
+// atom b (runs 4b .. 4b+7 added in order), scaled and rounded to bf16: the
+// order of compress_keys_kernel for both geometries, so either compressor
+// gives the same bits.  Each key is read by two neighbouring blocks (the
+// second read hits L2), where two separate compressions read it four times.
+
+__global__ void __launch_bounds__(256) compress_keys_dual_kernel(
+    const uint4* __restrict__ k, const int32_t* __restrict__ cu_k, const int32_t* __restrict__ cu_c,
+    const int32_t* __restrict__ cu_c2, int64_t total_k, int vecs_per_row,
+    uint4* __restrict__ kc, uint4* __restrict__ kc2, int32_t* status) {
+  const int b = blockIdx.y;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int blk = static_cast<int>(gid / vecs_per_row);
+  const int vec = static_cast<int>(gid % vecs_per_row);
+  const int64_t c0 = __ldg(cu_c + b), c20 = __ldg(cu_c2 + b);
+  const int atoms = static_cast<int>(__ldg(cu_c + b + 1) - c0);
+  const int atoms2 = static_cast<int>(__ldg(cu_c2 + b + 1) - c20);
+  // A 128/64 atom b needs keys [64b, 64b+128), so it implies the 32/16 atom 4b.
+  if (4 * blk >= atoms) return;
+  const bool has2 = blk < atoms2;
+  const int first = 4 * blk;
+  const int last = has2 ? first + 7 : min(first + 4, atoms);  // last run read
+  const int64_t tok0 = __ldg(cu_k + b) + static_cast<int64_t>(first) * 16;
+  if (tok0 + static_cast<int64_t>(last - first + 1) * 16 > total_k) {
+    report(status, LS_DEVERR_SEQLENS);
+    return;
+  }
+  const uint4* src = k + tok0 * vecs_per_row + vec;
+  float prev[8], acc2[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) prev[c] = acc2[c] = 0.f;
+  for (int j = first; j <= last; ++j) {
+    float run[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) run[c] = 0.f;
+    const uint4* rs = src + static_cast<int64_t>(j - first) * 16 * vecs_per_row;
+#pragma unroll 4
+    for (int t = 0; t < 16; ++t) {
+      const uint4 u = __ldg(rs + static_cast<int64_t>(t) * vecs_per_row);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float2 f = __bfloat1622float2(h[c]);
+        run[2 * c] += f.x;
+        run[2 * c + 1] += f.y;
+      }
+    }
+    const int a = j - 1;  // the 32/16 atom that ends with this run
+    if (j > first && a < atoms && a <= first + 3) {
+      float acc[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[c] = (0.f + prev[c]) + run[c];
+      uint4 out;
+      out.x = pack_bf16x2(acc[0] * (1.f / 32.f), acc[1] * (1.f / 32.f));
+      out.y = pack_bf16x2(acc[2] * (1.f / 32.f), acc[3] * (1.f / 32.f));
+      out.z = pack_bf16x2(acc[4] * (1.f / 32.f), acc[5] * (1.f / 32.f));
+      out.w = pack_bf16x2(acc[6] * (1.f / 32.f), acc[7] * (1.f / 32.f));
+      kc[(c0 + a) * vecs_per_row + vec] = out;
+    }
+    if (has2) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc2[c] += run[c];
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) prev[c] = run[c];
+  }
+  if (has2) {
+    uint4 out;
+    out.x = pack_bf16x2(acc2[0] * (1.f / 128.f), acc2[1] * (1.f / 128.f));
+    out.y = pack_bf16x2(acc2[2] * (1.f / 128.f), acc2[3] * (1.f / 128.f));
+    out.z = pack_bf16x2(acc2[4] * (1.f / 128.f), acc2[5] * (1.f / 128.f));
+    out.w = pack_bf16x2(acc2[6] * (1.f / 128.f), acc2[7] * (1.f / 128.f));
+    kc2[(c20 + blk) * vecs_per_row + vec] = out;
+  }
+}
+
+cudaError_t launch_compress_keys_dual(const uint16_t* k, const int32_t* cu_k, const int32_t* cu_c,
+                                      const int32_t* cu_c2, int batch, int max_atoms,
+                                      int64_t total_k, int G, int D, uint16_t* kc, uint16_t* kc2,
+                                      int32_t* status, cudaStream_t stream) {
+  if (max_atoms <= 0) return cudaSuccess;
+  const int vecs = G * D / 8;
+  const int64_t threads = static_cast<int64_t>((max_atoms + 3) / 4) * vecs;
+  const dim3 grid(static_cast<unsigned>((threads + 255) / 256), static_cast<unsigned>(batch));
+  compress_keys_dual_kernel<<<grid, 256, 0, stream>>>(
+      reinterpret_cast<const uint4*>(k), cu_k, cu_c, cu_c2, total_k, vecs,
+      reinterpret_cast<uint4*>(kc), reinterpret_cast<uint4*>(kc2), status);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_compress_keys(const uint16_t* k, const int32_t* cu_k, const int32_t* cu_c,
                                  int batch, int64_t total_k, int64_t total_c, int G, int D,
                                  int kernel_size, int kernel_stride, uint16_t* kc,
@@ -246,12 +344,12 @@ cudaError_t launch_compress_keys(const uint16_t* k, const int32_t* cu_k, const i
   const int vecs = G * D / 8;
   const int64_t threads = total_c * vecs;
   const int64_t blocks = (threads + 255) / 256;
+  const int run_len = compress_run_length(kernel_stride);
   compress_keys_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
       reinterpret_cast<const uint4*>(k), cu_k, cu_c, batch, total_k, total_c, vecs,
-      kernel_size / kernel_stride, kernel_stride, 1.0f / static_cast<float>(kernel_size),
+      kernel_size / run_len, run_len, kernel_stride, 1.0f / static_cast<float>(kernel_size),
       reinterpret_cast<uint4*>(kc), status);
   return cudaGetLastError();
 }
-
 
 }  // namespace ls

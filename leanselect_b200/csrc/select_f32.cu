@@ -29,13 +29,14 @@ namespace ls {
 namespace {
 
 // ---------------------------------------------------------------------------
-// Compression: one thread per (atom, 4 channels), runs of `stride` keys summed
-// in order, the run sums added, scaled by 1/kernel_size (the oracle's order).
+// Compression: one thread per (atom, 4 channels), runs of `run_len` keys
+// summed in order, the run sums added, scaled by 1/kernel_size (the oracle's
+// order).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) compress_keys_f32_kernel(
     const float4* __restrict__ k, const int32_t* __restrict__ cu_k, const int32_t* __restrict__ cu_c,
-    int batch, int64_t total_k, int64_t total_c, int vecs_per_row, int runs, int stride,
-    float inv_kernel, float4* __restrict__ kc, int32_t* status) {
+    int batch, int64_t total_k, int64_t total_c, int vecs_per_row, int runs, int run_len,
+    int stride, float inv_kernel, float4* __restrict__ kc, int32_t* status) {
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t atom = gid / vecs_per_row;
   const int vec = static_cast<int>(gid % vecs_per_row);
@@ -43,7 +44,7 @@ __global__ void __launch_bounds__(256) compress_keys_f32_kernel(
   const int b = find_sequence(cu_c, batch, atom);
   const int64_t local = atom - __ldg(cu_c + b);
   const int64_t tok0 = __ldg(cu_k + b) + local * stride;
-  if (tok0 + static_cast<int64_t>(runs) * stride > total_k) {
+  if (tok0 + static_cast<int64_t>(runs) * run_len > total_k) {
     report(status, LS_DEVERR_SEQLENS);
     return;
   }
@@ -51,8 +52,8 @@ __global__ void __launch_bounds__(256) compress_keys_f32_kernel(
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int j = 0; j < runs; ++j) {
     float4 run = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int t = 0; t < stride; ++t) {
-      const float4 u = __ldg(src + (static_cast<int64_t>(j) * stride + t) * vecs_per_row);
+    for (int t = 0; t < run_len; ++t) {
+      const float4 u = __ldg(src + (static_cast<int64_t>(j) * run_len + t) * vecs_per_row);
       run.x += u.x;
       run.y += u.y;
       run.z += u.z;
@@ -328,7 +329,8 @@ int ls_compress_keys_f32(const float* k, const int32_t* cu_seqlens_k, int32_t ba
     const int64_t threads = total_c * vecs;
     compress_keys_f32_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(
         reinterpret_cast<const float4*>(k), cu_seqlens_k, cu_seqlens_c, batch, total_k, total_c,
-        vecs, kernel_size / kernel_stride, kernel_stride, 1.0f / static_cast<float>(kernel_size),
+        vecs, kernel_size / compress_run_length(kernel_stride), compress_run_length(kernel_stride),
+        kernel_stride, 1.0f / static_cast<float>(kernel_size),
         reinterpret_cast<float4*>(k_compressed), status);
     err = cudaGetLastError();
   }

@@ -14,6 +14,10 @@ nosa.py:1822-1853):
 
 * ``compress_k`` / ``compress_k2`` -> :class:`leanselect_b200.CompressK`
   (minicpm.py:2035-2046 instantiates them, 2476-2481 calls them);
+* ``get_compress_k`` -> the prefill branch computes both compressions in one
+  pass over the keys and fills the ``InfLLMv2Cache`` through its own
+  ``update_*`` methods, as minicpm.py:2782-2866 does; decode steps and the
+  KL-target caches keep the reference's method;
 * ``leanselect`` -> :class:`leanselect_b200.LeanSelectSelector` sharing the
   reference selector's parameter tensors;
 * ``_lightweight_compressed_attention`` -> the fused selection
@@ -25,8 +29,12 @@ The reference tree is not imported here; objects are matched by attribute.
 from __future__ import annotations
 
 import functools
+import sys
 import types
 
+import torch
+
+from . import ops
 from .attention import (CompressK, infllmv2_attn_stage1, infllmv2_attn_varlen_func,
                         lightweight_compressed_attention, max_pooling_1d_varlen,
                         nosa_atom_scores)
@@ -64,6 +72,48 @@ def _sparse_forward(self, query_layer, key_layer, value_layer, cu_seqlens_q, cu_
         causal=max_seqlen_in_batch_q != 1, topk_idx=topk_idx)
 
 
+def _get_compress_k(self, key_states, attention_mask, past_key_value,
+                    enable_kl_target_cache: bool = False):
+    """``MiniCPMInfLLMv2Attention.get_compress_k`` (minicpm.py:2774-2964).
+
+    Prefill: unpad the keys with the reference module's own
+    ``_unpad_one_tensor``, compute ``compress_k`` (32/16) and ``compress_k2``
+    (128/64) in one pass over K (``ops.compress_keys_dual``, bit for bit
+    what the two compressor modules give), and hand the cache the same
+    updates as minicpm.py:2794-2866: both compressions with their
+    cu_seqlens, and per sequence the keys after the last atom's start
+    (``A * kernel_stride`` on, resp. ``A2 * 4 * kernel_stride``) as the
+    uncompressed tails a decode step extends.  Decode steps, KL-target
+    caches and other geometries or dtypes call the reference method.
+    """
+    layer = past_key_value.layers[self.layer_idx]
+    prefilling = not layer.compress_k_cache
+    kl_target = enable_kl_target_cache and getattr(self, "_kl_target_compress_differs", False)
+    geometry = (int(self.kernel_size), int(self.kernel_stride)) == (32, 16)
+    if not prefilling or kl_target or not geometry or key_states.dtype != torch.bfloat16:
+        return self._reference_get_compress_k(key_states, attention_mask, past_key_value,
+                                              enable_kl_target_cache)
+    unpad = sys.modules[type(self).__module__]._unpad_one_tensor
+    unpadded, _, cu_seqlens, _ = unpad(key_states, attention_mask=attention_mask)
+    lengths = ops.host_lengths(cu_seqlens)
+    kc, cu_c, kc2, cu_c2 = ops.compress_keys_dual(unpadded, cu_seqlens, lengths=lengths)
+    past_key_value.update_compress_k(kc, self.layer_idx, cu_c)
+    past_key_value.update_compress_k2(kc2, self.layer_idx, cu_c2)
+    stride = int(self.kernel_stride)
+    starts = [0]
+    for n in lengths:
+        starts.append(starts[-1] + n)
+    tails = [unpadded[s0 + ops.atom_count(n, 32, 16) * stride:s0 + n].clone()
+             for s0, n in zip(starts, lengths)]
+    past_key_value.update_no_compress_k(tails, self.layer_idx, kernel_stride=stride,
+                                        kernel_size=int(self.kernel_size))
+    tails2 = [unpadded[s0 + ops.atom_count(n, 128, 64) * stride * 4:s0 + n].clone()
+              for s0, n in zip(starts, lengths)]
+    past_key_value.update_no_compress_k2(tails2, self.layer_idx, kernel_stride=stride * 4,
+                                         kernel_size=int(self.kernel_size) * 4)
+    return kc, cu_c, kc2, cu_c2
+
+
 def patch_attention(attn) -> None:
     """Patch one reference attention module in place."""
     heads_k = int(attn.num_key_value_heads)
@@ -76,6 +126,10 @@ def patch_attention(attn) -> None:
     attn._lightweight_compressed_attention = functools.partial(
         lightweight_compressed_attention, attn)
     attn.sparse_forward = types.MethodType(_sparse_forward, attn)
+    reference = getattr(attn, "get_compress_k", None)
+    if reference is not None and getattr(reference, "__func__", None) is not _get_compress_k:
+        attn._reference_get_compress_k = reference
+        attn.get_compress_k = types.MethodType(_get_compress_k, attn)
 
 
 def patch_selector_owner(owner) -> None:

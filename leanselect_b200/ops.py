@@ -219,6 +219,32 @@ def compress_keys(k: torch.Tensor, cu_seqlens_k: torch.Tensor, *, kernel_size: i
     return kc, cu_c
 
 
+def compress_keys_dual(k: torch.Tensor, cu_seqlens_k: torch.Tensor, *,
+                       lengths: Sequence[int] | None = None):
+    """``compress_k`` (32/16) and ``compress_k2`` (128/64) of one prefill in one pass over K.
+
+    Returns ``(kc, cu_c, kc2, cu_c2)``, bit for bit what :func:`compress_keys`
+    gives for the two geometries (minicpm.py:2785-2792).
+    """
+    dev = _require_cuda(k, cu_seqlens_k)
+    if k.ndim != 3:
+        raise ValueError("k must be [total_k, num_kv_heads, head_dim]")
+    kb = _bf16(k)
+    cu = _i32(cu_seqlens_k)
+    lens = list(lengths) if lengths is not None else host_lengths(cu)
+    total_c = sum(atom_count(n, 32, 16) for n in lens)
+    total_c2 = sum(atom_count(n, 128, 64) for n in lens)
+    g, d = k.shape[1], k.shape[2]
+    kc = torch.empty(total_c, g, d, dtype=torch.bfloat16, device=dev)
+    kc2 = torch.empty(total_c2, g, d, dtype=torch.bfloat16, device=dev)
+    cu_c, cu_c2 = torch.empty_like(cu), torch.empty_like(cu)
+    _call(dev, "ls_compress_keys_dual", kb.data_ptr(), cu.data_ptr(), cu.numel() - 1,
+          max(lens, default=0), kb.shape[0], g, d, _ptr(kc) if total_c else None,
+          cu_c.data_ptr(), total_c, _ptr(kc2) if total_c2 else None, cu_c2.data_ptr(), total_c2,
+          status_word(dev).data_ptr(), _stream(dev))
+    return kc, cu_c, kc2, cu_c2
+
+
 # ---------------------------------------------------------------------------
 # a3/a4: projections
 # ---------------------------------------------------------------------------

@@ -153,7 +153,8 @@ def _comm_stream(dev: torch.device) -> torch.cuda.Stream:
 
 def sequence_parallel_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_len: int,
                             selector, cfg, group=None, timers: list | None = None,
-                            key_counts: list | None = None) -> torch.Tensor:
+                            key_counts: list | None = None,
+                            capture: dict | None = None) -> torch.Tensor:
     """The hot path of one layer for this rank's two zig-zag query chunks.
 
     ``q [2C, H, D]``, ``k``/``v [2C, G, D]`` are this rank's rows (chunk ``r``
@@ -171,7 +172,9 @@ def sequence_parallel_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s
     late chunk selected and attended.
     The result equals gathering everything first.  ``timers`` receives
     ``(stage, start, end)`` CUDA events for "gather", "compress", "select" and
-    "attn" (two spans per stage: early chunk, late chunk).
+    "attn" (two spans per stage: early chunk, late chunk); ``capture``
+    (optional dict) receives the page lists of the two chunks as ``idx``
+    ``[G, 2C, T]`` (this rank's rows, in its local order).
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -265,6 +268,8 @@ def sequence_parallel_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s
         if timers is not None:
             timers.append(("gather", e_w0, e_w1))
     idx1 = chunk_work(1, n)
+    if capture is not None:
+        capture["idx"] = torch.cat((idx0, idx1), dim=1)
     if key_counts is not None:
         positions = local_positions(n, world, rank, device=dev)
         total = 0

@@ -1,8 +1,8 @@
 """Batched small-model prefill, data-parallel (benchmark config 4).
 
-    python -m leanselect_b200.batched [--sequences 64] [--steps 2] [--warmup 1]
+    python -m measure.batched [--sequences 64] [--steps 2] [--warmup 1]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
-        -m leanselect_b200.batched ...          # data-parallel over N GPUs
+        -m measure.batched ...          # data-parallel over N GPUs
 
 Random-init 24-layer model (hidden 2048, 16 query / 2 KV heads, head_dim
 128), a batch of ``--sequences`` sequences of uniform-random token ids with
@@ -23,9 +23,9 @@ import os
 
 import torch
 
-from .attention import LayerConfig, config4_budget
-from .model import MiniCPMShape
-from .parallel import DataParallelRunner, lpt_shards
+from leanselect_b200.attention import LayerConfig, config4_budget
+from leanselect_b200.model import MiniCPMShape
+from leanselect_b200.parallel import DataParallelRunner, lpt_shards
 
 
 def batch_lengths(sequences: int, seed: int, lo: int = 8192, hi: int = 32768) -> list[int]:

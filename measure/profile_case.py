@@ -1,6 +1,6 @@
 """One layer of the hot path on synthetic inputs, for profilers.
 
-    python -m leanselect_b200.profile_case [--seq-len 32768] [--topk 67] [--repeat 1]
+    python -m measure.profile_case [--seq-len 32768] [--topk 67] [--repeat 1]
 
 Builds benchmark config-1-shaped inputs (32 query / 2 KV heads, head_dim 128,
 N(0,1) q/k/v, selector with a 32x4 router) on ``cuda:0`` and runs
@@ -14,7 +14,7 @@ import argparse
 
 import torch
 
-from . import LeanSelectSelector, ops
+from leanselect_b200 import LeanSelectSelector, ops
 
 
 def main(argv=None) -> int:

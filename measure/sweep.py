@@ -1,9 +1,9 @@
 """Sequence-length sweep of one hot-path layer (benchmark config 3).
 
-    python -m leanselect_b200.sweep [--lengths 32768,65536,131072,262144,524288] [--reps 3]
+    python -m measure.sweep [--lengths 32768,65536,131072,262144,524288] [--reps 3]
                                     [--method leanselect|uniform]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
-        -m leanselect_b200.sweep ...            # sequence-parallel over N GPUs
+        -m measure.sweep ...            # sequence-parallel over N GPUs
 
 One benchmark config-1 layer (bf16, 32 query / 2 KV heads, head_dim 128,
 budget 64 pages + sink + 2 local pages of 64 tokens) at each length, with
@@ -23,48 +23,17 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 
 import torch
 
-from . import LeanSelectSelector, ops
-from .attention import LayerConfig, prefill_layer_attention
+from leanselect_b200 import ops
+from leanselect_b200.attention import LayerConfig, prefill_layer_attention
+
+from .inputs import config1_layer, make_selector
 
 STAGES = ("gather", "compress", "select", "attn")
-
-
-def config1_layer(n: int, device: torch.device, seed: int = 0, num_heads: int = 32,
-                  num_kv_heads: int = 2, head_dim: int = 128, hot_pages: int = 24,
-                  hot_shift: float = 0.5):
-    """benchmark config-0/1 distribution for one sequence of ``n`` tokens, on ``device``."""
-    g = torch.Generator(device=device).manual_seed(seed)
-    q = torch.randn(n, num_heads, head_dim, device=device, generator=g)
-    k = torch.randn(n, num_kv_heads, head_dim, device=device, generator=g)
-    v = torch.randn(n, num_kv_heads, head_dim, device=device, generator=g)
-    u = torch.randn(head_dim, device=device, generator=g)
-    u /= u.norm()
-    pages = (n + 63) // 64
-    for kv in range(num_kv_heads):
-        hot = torch.randperm(pages, device=device, generator=g)[:hot_pages]
-        rows = (hot[:, None] * 64 + torch.arange(64, device=device)[None, :]).reshape(-1)
-        rows = rows[rows < n]
-        k[rows, kv] += hot_shift * u
-    q += hot_shift * u
-    return q.bfloat16(), k.bfloat16(), v.bfloat16()
-
-
-def make_selector(device: torch.device, seed: int = 0, num_heads: int = 32,
-                  num_kv_heads: int = 2) -> LeanSelectSelector:
-    with torch.random.fork_rng(devices=[]):
-        torch.manual_seed(seed)  # the projections' own initialisation, identical on every rank
-        sel = LeanSelectSelector(num_heads=num_heads, num_kv_heads=num_kv_heads, head_dim=128,
-                                 router_heads=32, router_dim=4)
-    gen = torch.Generator().manual_seed(seed + 1)
-    with torch.no_grad():
-        sel.head_mix.copy_(torch.randn(sel.head_mix.shape, generator=gen) / math.sqrt(32))
-    return sel.to(device)
 
 
 def run_length(n: int, reps: int, device: torch.device, dist=None, seed: int = 0,
@@ -77,7 +46,7 @@ def run_length(n: int, reps: int, device: torch.device, dist=None, seed: int = 0
     q, k, v = config1_layer(n, device, seed)
     sel = make_selector(device, seed)
     if world > 1:
-        from .parallel import sequence_parallel_layer, zigzag_chunks
+        from leanselect_b200.parallel import sequence_parallel_layer, zigzag_chunks
 
         chunks = zigzag_chunks(n, world, rank)
         q = torch.cat([q[a:a + c] for a, c in chunks]).contiguous()

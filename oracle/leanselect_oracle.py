@@ -139,12 +139,13 @@ def compress_keys(k: np.ndarray, cu_seqlens_k: np.ndarray, *, kernel_size: int =
     ``cu_seqlens_compressed``.  The same math as ``pages.compress_keys_mean``
     (pages.py:84-101) for sequences of at least ``kernel_size`` tokens.
 
-    Summation order: the window is split into ``kernel_size // kernel_stride``
-    runs of ``kernel_stride`` tokens; each run is summed sequentially in fp32,
-    the run sums are added in order and the total is multiplied by
-    ``1/kernel_size`` (exact for powers of two) before the optional bf16
-    rounding.  The CUDA kernel uses the same order, so in ``bf16`` policy the
-    two agree bit for bit.
+    Summation order: the window is split into runs of ``run`` tokens, where
+    ``run`` is 16 when 16 divides ``kernel_stride`` and ``kernel_stride``
+    otherwise; each run is summed sequentially in fp32, the run sums are
+    added in order and the total is multiplied by ``1/kernel_size`` (exact
+    for powers of two) before the optional bf16 rounding.  The CUDA kernels
+    use the same order (16-key runs let one pass serve the 32/16 and 128/64
+    compressions together), so in ``bf16`` policy they agree bit for bit.
     """
     k = np.asarray(k, dtype=np.float32)
     if k.ndim != 3:
@@ -155,25 +156,26 @@ def compress_keys(k: np.ndarray, cu_seqlens_k: np.ndarray, *, kernel_size: int =
     total_c = int(cu_c[-1])
     g, d = k.shape[1:]
     out = np.zeros((total_c, g, d), dtype=np.float32)
-    runs = kernel_size // kernel_stride
+    run_len = 16 if kernel_stride % 16 == 0 else kernel_stride
+    runs = kernel_size // run_len            # runs per window
+    step = kernel_stride // run_len          # runs between window starts
     inv = np.float32(1.0 / kernel_size)
     cu = np.asarray(cu_seqlens_k, dtype=np.int64)
     for b in range(len(cu) - 1):
-        start, end = int(cu[b]), int(cu[b + 1])
+        start = int(cu[b])
         n_atoms = int(cu_c[b + 1] - cu_c[b])
         if n_atoms == 0:
             continue
-        n_runs = n_atoms - 1 + runs
-        seq = k[start:start + n_runs * kernel_stride]
-        # Sequential fp32 sum inside each run of kernel_stride tokens.
+        n_runs = (n_atoms - 1) * step + runs
+        seq = k[start:start + n_runs * run_len]
+        # Sequential fp32 sum inside each run of run_len tokens.
         run = np.zeros((n_runs, g, d), dtype=np.float32)
-        for i in range(kernel_stride):
-            run += seq[i::kernel_stride][:n_runs]
+        for i in range(run_len):
+            run += seq[i::run_len][:n_runs]
         acc = np.zeros((n_atoms, g, d), dtype=np.float32)
         for j in range(runs):
-            acc += run[j:j + n_atoms]
+            acc += run[j:j + (n_atoms - 1) * step + 1:step]
         out[int(cu_c[b]):int(cu_c[b + 1])] = acc * inv
-        del end
     return _maybe_round(out, policy), cu_c
 
 

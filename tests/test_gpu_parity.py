@@ -347,7 +347,7 @@ def test_long_rows_take_the_global_path_exact_ties():
     from the workspace instead of the per-warp shared-memory copy.  With a
     zero head mix every score ties, so the answer is known for every row:
     the sinks, the lowest candidate pages, the local pages."""
-    from leanselect_b200.sweep import config1_layer, make_selector
+    from measure.inputs import config1_layer, make_selector
 
     n, T = 147456, 67
     q, _, _ = config1_layer(n, DEV, 6)
@@ -417,7 +417,7 @@ def test_full_size_selection_properties_and_row_parity():
     nothing past the query's page (test_runtime.py:71-94 checks the same
     visibility), the sink and the three local pages always present.  A row
     sample then matches the oracle's selection and attention."""
-    from leanselect_b200.sweep import config1_layer, make_selector
+    from measure.inputs import config1_layer, make_selector
 
     n, T = 131072, 67
     q, k, v = config1_layer(n, DEV, 5)
@@ -927,3 +927,114 @@ def test_config0_attention_against_fp32_oracle():
     assert out.dtype == torch.float32
     ref = ora.attention_for_queries(inp.q[rows], rows, inp.k, inp.v, sel.topk_idx)
     _attn_check(out[torch.from_numpy(rows).to(DEV)], None, ref, None)
+
+
+# ---------------------------------------------------------------------------
+# f1: both compressions in one pass, and the decode cache they fill
+# ---------------------------------------------------------------------------
+
+def _unpad_one_tensor(hidden_states, attention_mask):
+    """The unpad the reference's get_compress_k uses (minicpm.py:753-769):
+    rows where the mask is set, with int32 cu_seqlens; found by the patched
+    method in the module of the attention class, as in the reference."""
+    seqlens = attention_mask.sum(dim=-1, dtype=torch.int32)
+    indices = torch.nonzero(attention_mask.flatten(), as_tuple=False).flatten()
+    cu = torch.nn.functional.pad(torch.cumsum(seqlens, dim=0, dtype=torch.int32), (1, 0))
+    b, s = hidden_states.shape[:2]
+    flat = hidden_states.reshape(b * s, *hidden_states.shape[2:])
+    return flat[indices], indices, cu, int(seqlens.max().item())
+
+
+class _CacheLayer:
+    def __init__(self):
+        self.compress_k_cache = []
+
+
+class _InfLLMv2Cache:
+    """Records the updates InfLLMv2Cache receives (minicpm.py:1417-1445)."""
+
+    def __init__(self, layers):
+        self.layers = [_CacheLayer() for _ in range(layers)]
+        self.calls = {}
+
+    def update_compress_k(self, key_states, layer_idx, cu_seqlens=None, cache_kwargs=None):
+        self.calls["k"] = (key_states, cu_seqlens)
+        self.layers[layer_idx].compress_k_cache.append(key_states)
+
+    def update_compress_k2(self, key_states, layer_idx, cu_seqlens=None, cache_kwargs=None):
+        self.calls["k2"] = (key_states, cu_seqlens)
+
+    def update_no_compress_k(self, key_states, layer_idx, kernel_size=32, kernel_stride=16,
+                             cache_kwargs=None):
+        self.calls["tail"] = (key_states, kernel_size, kernel_stride)
+
+    def update_no_compress_k2(self, key_states, layer_idx, kernel_size=128, kernel_stride=64,
+                              cache_kwargs=None):
+        self.calls["tail2"] = (key_states, kernel_size, kernel_stride)
+
+
+class MiniCPMInfLLMv2Attention(torch.nn.Module):
+    """The attributes of the reference attention the shim reads."""
+
+    def __init__(self):
+        super().__init__()
+        self.num_key_value_heads, self.head_dim = 2, 128
+        self.kernel_size, self.kernel_stride = 32, 16
+        self.compress_k = torch.nn.Identity()
+        self.compress_k2 = torch.nn.Identity()
+        self.layer_idx = 0
+        self.reference_calls = 0
+
+    def get_compress_k(self, key_states, attention_mask, past_key_value,
+                       enable_kl_target_cache=False):
+        self.reference_calls += 1
+        return None
+
+
+@pytest.mark.parametrize("lens", [[3000, 700, 129, 20, 1500], [131]])
+def test_dual_compression_fills_the_prefill_cache(lens):
+    """The patched get_compress_k (prefill) compresses K once for compress_k
+    (32/16) and compress_k2 (128/64): both bit-exact with the oracle and with
+    the patched compressor modules, tails = keys from A*16 (A2*64) on, and
+    the same cache updates as minicpm.py:2794-2866; a decode step goes to
+    the reference method."""
+    from leanselect_b200 import integration
+
+    inp = ora.synthetic_layer(lens, num_heads=4, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=2, seed=33, bf16=True)
+    b, s = len(lens), max(lens)
+    keys = torch.zeros(b, s, 2, 128, dtype=torch.bfloat16, device=DEV)
+    mask = torch.zeros(b, s, dtype=torch.int32, device=DEV)
+    for i, n in enumerate(lens):   # left-padded, as generation batches are
+        keys[i, s - n:] = to_dev(inp.k[inp.cu_seqlens[i]:inp.cu_seqlens[i + 1]])
+        mask[i, s - n:] = 1
+    attn = MiniCPMInfLLMv2Attention()
+    integration.patch_attention(attn)
+    cache = _InfLLMv2Cache(1)
+    kc, cu_c, kc2, cu_c2 = attn.get_compress_k(keys, mask, cache)
+    assert attn.reference_calls == 0
+    ekc, ecu = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    ekc2, ecu2 = ora.compress_keys(inp.k, inp.cu_seqlens, kernel_size=128, kernel_stride=64,
+                                   policy="bf16")
+    np.testing.assert_array_equal(kc.float().cpu().numpy(), ekc)
+    np.testing.assert_array_equal(kc2.float().cpu().numpy(), ekc2)
+    np.testing.assert_array_equal(cu_c.cpu().numpy(), ecu)
+    np.testing.assert_array_equal(cu_c2.cpu().numpy(), ecu2)
+    assert cache.calls["k"][0] is kc and cache.calls["k2"][0] is kc2
+    kflat = to_dev(inp.k)
+    cu_k = cu_dev(inp.cu_seqlens)
+    m1, mc1 = attn.compress_k(kflat, cu_k)
+    m2, mc2 = attn.compress_k2(kflat, cu_k)
+    assert torch.equal(m1, kc) and torch.equal(m2, kc2)
+    assert torch.equal(mc1, cu_c) and torch.equal(mc2, cu_c2)
+    tails, size, stride = cache.calls["tail"]
+    tails2, size2, stride2 = cache.calls["tail2"]
+    assert (size, stride, size2, stride2) == (32, 16, 128, 64)
+    for i, n in enumerate(lens):
+        seq = kflat[inp.cu_seqlens[i]:inp.cu_seqlens[i + 1]]
+        assert torch.equal(tails[i], seq[ora.atom_count(n) * 16:])
+        assert torch.equal(tails2[i], seq[ora.atom_count(n, 128, 64) * 64:])
+    # A decode step (the cache already holds compressed keys) is the reference's.
+    attn.get_compress_k(keys[:, -1:], mask, cache)
+    assert attn.reference_calls == 1
+    assert ops.check_status(DEV) == 0

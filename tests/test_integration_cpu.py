@@ -35,6 +35,11 @@ class MiniCPMInfLLMv2Attention(nn.Module):
         self.leanselect = RefSelector()
         self.topk, self.block_size, self.init_blocks, self.local_blocks = 67, 64, 1, 2
         self.selection_method = "leanselect"
+        self.layer_idx = 0
+
+    def get_compress_k(self, key_states, attention_mask, past_key_value,
+                       enable_kl_target_cache=False):
+        return "reference"
 
 
 class NosaAttention(nn.Module):
@@ -56,6 +61,11 @@ def test_install_patches_every_attention_module():
         assert isinstance(attn.leanselect, lsb.LeanSelectSelector)
         assert attn._lightweight_compressed_attention.func is lsb.lightweight_compressed_attention
         assert isinstance(attn.sparse_forward, types.MethodType)
+        assert attn.get_compress_k.__func__ is integration._get_compress_k
+        assert attn._reference_get_compress_k(None, None, None) == "reference"
+    # Installing twice keeps the reference method, not the patched one.
+    integration.install(model)
+    assert model[0]._reference_get_compress_k(None, None, None) == "reference"
     assert isinstance(model[2].leanselect, lsb.LeanSelectSelector)
     assert model[2]._leanselect_atom_scores.func is lsb.nosa_atom_scores
     # The selectors share the reference parameter tensors (checkpoints keep working).

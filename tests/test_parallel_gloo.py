@@ -96,7 +96,7 @@ def test_config4_budget_rule():
 
 
 def test_config4_batch_lengths_are_seeded_and_in_range():
-    from leanselect_b200.batched import batch_lengths
+    from measure.batched import batch_lengths
     a, b = batch_lengths(64, 0), batch_lengths(64, 0)
     assert a == b and len(a) == 64
     assert all(8192 <= n <= 32768 for n in a)

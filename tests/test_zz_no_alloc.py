@@ -71,7 +71,7 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(first, secon
 def test_noalloc_accepts_a_request_of_exactly_its_scratch():
     """One 16384-token sequence with 2 KV groups needs exactly the 16 MiB built
     into the library: accepted, and equal to the workspace entry point."""
-    from leanselect_b200.sweep import config1_layer, make_selector
+    from measure.inputs import config1_layer, make_selector
 
     n = 16384
     lib = _native.load()
