@@ -165,6 +165,21 @@ int ls_score_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
                    int32_t kernel_stride, float* page_scores, int32_t* status, void* stream);
 
 /*
+ * ls_score_pages_single -- LeanSelectSelector.score_pages for one sequence
+ * with the reference's own seq_len argument (leanselect/selector.py:192-214):
+ * q [total_q, H, D] are any query rows, ks [G, total_c, F] the sequence's
+ * atoms, and the output has ceil(seq_len/64) pages per row whatever
+ * total_q is: page p pools atoms [4p-1, 4p+4) that exist (no causal mask),
+ * pages with no atom are -inf.  Values as ls_score_pages (bf16 numbers in
+ * fp32).  page_scores [G, total_q, ceil(seq_len/64)] fp32.
+ */
+int ls_score_pages_single(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                          int64_t total_q, int64_t total_c, int32_t seq_len, int32_t num_heads,
+                          int32_t num_kv_heads, int32_t head_dim, int32_t width,
+                          int32_t block_size, int32_t kernel_stride, float* page_scores,
+                          int32_t* status, void* stream);
+
+/*
  * ls_atom_scores -- replaces NOSA's LlamaSdpaAttention._leanselect_atom_scores
  * (leanselect/models/nosa.py:1822-1853): raw LeanSelect atom scores
  * Qs[t]·Ks[a] for every (group, query row, atom of its sequence), no causal

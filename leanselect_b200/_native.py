@@ -41,6 +41,8 @@ SIGNATURES = {
     "ls_project_queries": [_P, _I64, _I32, _I32, _I32, _P, _I32, _P, _P, _P],
     "ls_score_pages": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _I32,
                        _I32, _P, _P, _P],
+    "ls_score_pages_single": [_P, _P, _P, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
+                              _P, _P, _P],
     "ls_atom_scores": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _I32,
                        _P, _P, _P],
     "ls_select_pages": [_P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _I32,

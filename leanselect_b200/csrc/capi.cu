@@ -321,6 +321,38 @@ int ls_score_pages(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
   return err == cudaSuccess ? LS_OK : cuda_fail(err, "score_pages launch");
 }
 
+int ls_score_pages_single(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
+                          int64_t total_q, int64_t total_c, int32_t seq_len, int32_t num_heads,
+                          int32_t num_kv_heads, int32_t head_dim, int32_t width,
+                          int32_t block_size, int32_t kernel_stride, float* page_scores,
+                          int32_t* status, void* stream) {
+  int rc = check_score_common(q, wq_t, total_q, num_heads, num_kv_heads, head_dim, width);
+  if (rc != LS_OK) return rc;
+  LS_REQUIRE(total_c >= 0 && seq_len >= 0, "bad sizes");
+  if (block_size != 64 || kernel_stride != 16)
+    return fail(LS_ERR_UNSUPPORTED, "block_size must be 64 and kernel_stride 16");
+  if (seq_len > 65536 * 64)
+    return fail(LS_ERR_UNSUPPORTED, "sequences longer than 4M tokens are not supported");
+  if (total_q == 0 || seq_len == 0) return LS_OK;
+  LS_REQUIRE(page_scores, "null page_scores");
+  LS_REQUIRE(total_c == 0 || ks, "null ks");
+  if (ks) LS_REQUIRE_ALIGNED(ks);
+  ScoreArgs a{};
+  rc = build_score_args(&a, q, wq_t, ks, total_q, total_c, num_heads, num_kv_heads);
+  if (rc != LS_OK) return rc;
+  // One sequence: all total_q rows, all total_c atoms, ceil(seq_len/64) pages.
+  a.cu_q = nullptr;
+  a.cu_c = nullptr;
+  a.batch = 1;
+  a.max_seqlen_q = static_cast<int>(total_q);
+  a.seq_len = seq_len;
+  a.max_pages = (seq_len + 63) / 64;
+  a.page_scores = page_scores;
+  a.status = status;
+  const cudaError_t err = launch_score(kModeScore, a, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? LS_OK : cuda_fail(err, "score_pages_single launch");
+}
+
 int ls_atom_scores(const uint16_t* q, const uint16_t* wq_t, const uint16_t* ks,
                    const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_c, int32_t batch,
                    int32_t max_seqlen_q, int64_t total_q, int64_t total_c, int32_t num_heads,

@@ -649,13 +649,15 @@ __device__ int select_row(const Src& src, const GlobalChunks& row, int off, int 
     const int c = base + lane;
     if (c < nch) {
       const uint4 v = src.chunk(c);
+      const int first = 8 * c - off;
+      const bool full = first >= 0 && first + 8 <= m;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const int i = 8 * c + e - off;
-        if (i >= 0 && i < m) {
+        if (full || (first + e >= 0 && first + e < m)) {
           ++sampled;
           const float x = bf16_value(chunk_bits(v, e));
-          if (x > -INFINITY && x < INFINITY) {
+          // fminf / fmaxf drop NaN; infinities are left out of the range.
+          if (fabsf(x) < INFINITY) {
             smin = fminf(smin, x);
             smax = fmaxf(smax, x);
           }
@@ -737,18 +739,25 @@ __device__ int select_row(const Src& src, const GlobalChunks& row, int off, int 
   const uint32_t cut_bits =
       cut > -INFINITY ? static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_ru(cut)))
                       : 0xFF7Fu;
+  // Kept keys are >= the cut's key; their maximum is tracked on the way.
+  uint32_t kept_max = 0u;
   const int kept = compact_ge(
       src, off, m, as_bf162(cut_bits | (cut_bits << 16)),
       [&](int pos, uint32_t bits, int i) {
-        if (pos < kKeptCap) ws->kept[pos] = bf16_key(bits) << 16 | static_cast<uint32_t>(i);
+        const uint32_t key = bf16_key(bits);
+        kept_max = max(kept_max, key);
+        if (pos < kKeptCap) ws->kept[pos] = key << 16 | static_cast<uint32_t>(i);
       },
       lane);
   __syncwarp();
   release();
   int need = cap;
   if (kept >= cap && kept <= kKeptCap) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) kept_max = max(kept_max, __shfl_xor_sync(0xffffffffu, kept_max, o));
     const KeptKeys kk{ws->kept};
-    const uint32_t thr = radix_threshold(kk, kept, need, ws->hist, lane);
+    const uint32_t thr = radix_threshold_in(kk, kept, need, ws->hist, lane,
+                                            max(1u, bf16_key(cut_bits)), kept_max);
     return emit_threshold(kk, KeptIndex{ws->kept}, kept, thr, need, skip, n_init, out, k_out, lane);
   }
   // ---- exact radix over the whole row (the estimate kept too few or too many).

@@ -83,22 +83,10 @@ __device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
 // keys: at most 4).  Returns the threshold key;
 // `need` becomes the number of keys equal to it that belong to the
 // selection (the lowest indices win).
+// `kmin`/`kmax` bound the nonzero keys (any bounds that hold are fine).
 template <class Keys>
-__device__ uint32_t radix_threshold(const Keys& keys, int count, int& need, uint32_t* hist,
-                                      int lane) {
-  uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
-  for (int i = lane; i < count; i += 32) {
-    const uint32_t key = keys(i);
-    if (key != 0u) {
-      kmin = min(kmin, key);
-      kmax = max(kmax, key);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
-    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
-  }
+__device__ uint32_t radix_threshold_in(const Keys& keys, int count, int& need, uint32_t* hist,
+                                       int lane, uint32_t kmin, uint32_t kmax) {
   const uint32_t range = kmax - kmin;
   int shift = range > 255u ? (32 - __clz(range)) - 8 : 0;  // (range >> shift) < 256
   uint32_t lo = kmin;        // keys of the current pass: [lo, lo + width)
@@ -155,6 +143,26 @@ __device__ uint32_t radix_threshold(const Keys& keys, int count, int& need, uint
     width = uint64_t{1} << shift;   // the bin's keys, split into 256 again
     shift = max(0, shift - 8);
   }
+}
+
+// radix_threshold_in with the keys' own bounds, found by one pass.
+template <class Keys>
+__device__ uint32_t radix_threshold(const Keys& keys, int count, int& need, uint32_t* hist,
+                                    int lane) {
+  uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+  for (int i = lane; i < count; i += 32) {
+    const uint32_t key = keys(i);
+    if (key != 0u) {
+      kmin = min(kmin, key);
+      kmax = max(kmax, key);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+  }
+  return radix_threshold_in(keys, count, need, hist, lane, kmin, kmax);
 }
 
 // Writes, in index order, the entries among keys(0 .. count-1) above `thr`

@@ -304,6 +304,29 @@ def score_pages(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
     return out
 
 
+def score_pages_single(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor, seq_len: int,
+                       *, block_size: int = 64, kernel_stride: int = 16) -> torch.Tensor:
+    """Page scores ``[G, N, ceil(seq_len/64)]`` of query rows against one sequence's atoms.
+
+    The reference's ``score_pages`` with its own ``seq_len`` (selector.py:192-214):
+    the page count follows ``seq_len``, not the number of query rows.
+    """
+    dev = _require_cuda(q, ks)
+    qb = _bf16(q)
+    total_q = qb.shape[0]
+    G = weights.num_kv_heads
+    total_c = ks.shape[1]
+    pages = (int(seq_len) + block_size - 1) // block_size
+    out = torch.empty(G, total_q, pages, dtype=torch.float32, device=dev)
+    if total_q == 0 or pages == 0:
+        return out
+    _call(dev, "ls_score_pages_single", qb.data_ptr(), weights.wq_t.data_ptr(),
+          _ptr(ks) if total_c else None, total_q, total_c, int(seq_len), weights.num_heads, G,
+          weights.head_dim, weights.width, block_size, kernel_stride, out.data_ptr(),
+          status_word(dev).data_ptr(), _stream(dev))
+    return out
+
+
 def atom_scores(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor,
                 cu_seqlens_q: torch.Tensor, cu_seqlens_c: torch.Tensor, max_seqlen_q: int,
                 max_atoms: int) -> torch.Tensor:

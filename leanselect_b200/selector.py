@@ -125,23 +125,20 @@ class LeanSelectSelector(nn.Module):
                     block_size: int, kernel_stride: int) -> torch.Tensor:
         """Pooled page scores ``[G, N, ceil(seq_len/block_size)]`` (selector.py:192-214).
 
-        The B200 kernel pools over the query count: ``seq_len`` must equal
-        ``query.shape[0]`` (the only way the reference calls it,
-        minicpm.py:3117-3123).
+        As the reference: the page count follows ``seq_len`` (any number of
+        query rows), page ``p`` pools the atoms of its window that exist,
+        and pages without an atom are ``-inf``.
         """
         if query.ndim != 3 or tuple(query.shape[1:]) != (self.num_heads, self.head_dim):
             raise ValueError("query must have shape [N, num_heads, head_dim]")
         if compressed_keys.ndim != 3 or tuple(compressed_keys.shape[1:]) != (
                 self.num_kv_heads, self.head_dim):
             raise ValueError("compressed_keys must have shape [A, num_kv_heads, head_dim]")
-        n = int(query.shape[0])
-        if int(seq_len) != n:
-            raise ValueError("seq_len must equal the number of queries")
+        if min(int(seq_len), int(block_size), int(kernel_stride)) <= 0:
+            raise ValueError("page geometry must be positive")   # pages.py:163-164
         weights = self.kernel_weights()
         ks = ops.project_atom_keys(compressed_keys.detach(), weights.wk_t)
-        dev = query.device
-        cu_q = torch.tensor([0, n], dtype=torch.int32, device=dev)
-        cu_c = torch.tensor([0, compressed_keys.shape[0]], dtype=torch.int32, device=dev)
-        pages = ops.score_pages(query.detach(), weights, ks, cu_q, cu_c, n, block_size=block_size,
-                                kernel_stride=kernel_stride)
+        pages = ops.score_pages_single(query.detach(), weights, ks, int(seq_len),
+                                       block_size=int(block_size),
+                                       kernel_stride=int(kernel_stride))
         return pages if query.dtype == torch.float32 else pages.to(query.dtype)

@@ -176,6 +176,22 @@ def test_score_pages_single_sequence_api():
     _scores_close(got, want)
 
 
+@pytest.mark.parametrize("seq_len", [1500, 4000, 640, 1])
+def test_score_pages_with_its_own_seq_len(seq_len):
+    """The reference's score_pages takes seq_len apart from the query count
+    (selector.py:192-214): 1500 queries scored against 93 atoms with 1500,
+    4000 (pages past the atoms are -inf), 640 and 1 tokens' worth of pages."""
+    inp = ora.synthetic_layer([1500], num_heads=32, num_kv_heads=2, head_dim=128, router_heads=32,
+                              router_dim=4, hot_pages=5, seed=25, bf16=True)
+    sel = selector_for(inp.params)
+    kc, _ = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    got = sel.score_pages(to_dev(inp.q), to_dev(kc), seq_len=seq_len, block_size=64,
+                          kernel_stride=16).float().cpu().numpy()
+    want = ora.score_pages(inp.q, kc, inp.params, seq_len=seq_len, policy="bf16")
+    assert got.shape == want.shape == (2, 1500, (seq_len + 63) // 64)
+    _scores_close(got, want)
+
+
 def test_score_pages_packed_batch():
     lens = [700, 64, 65, 20, 1300]
     inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
