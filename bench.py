@@ -35,6 +35,14 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "prefill tokens/sec @128K (8B shape); select+attn ms/layer"
+# DRAM bytes (read + write) of one sparse-attention launch at 131072 tokens,
+# from a committed ncu capture: ncu cannot run inside the timed bench, and a
+# multi-pass capture of the 32-layer model would not fit the profiling rules.
+ATTN_TRAFFIC_BYTES = 6473.8e6 + 1071.2e6
+ATTN_TRAFFIC_SOURCE = (
+    "ncu dram__bytes_read.sum + dram__bytes_write.sum of sparse_attn_kernel<16> at 131072 tokens "
+    "(python -m measure.profile_case --seq-len 131072, the config-1 layer: same kernel, length "
+    "and budget as one bench layer), one-pass capture; summary committed under profiles/")
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -437,11 +445,8 @@ def run_ours(args):
             "peak_kind": f"{pk_kind} (bf16 dense, sustained)",
             "flops_per_layer": flops_per_layer,
             "attn_launches_per_layer": chunks,
-            # dram__bytes_read.sum + dram__bytes_write.sum per attention launch of
-            # this command at 131072 tokens: mean of 24 launches captured in one
-            # ncu pass (`--metrics gpu__time_duration.sum,dram__bytes_read.sum,
-            # dram__bytes_write.sum`, 4 layers).
-            "traffic": 6650.1e6 + 1070.9e6,
+            "traffic": ATTN_TRAFFIC_BYTES,
+            "traffic_source": ATTN_TRAFFIC_SOURCE,
         },
         "clocks": clocks.summary(),
     }
