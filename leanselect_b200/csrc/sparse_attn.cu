@@ -238,7 +238,9 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
 #pragma unroll
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  const float sl2 = args.scale_log2;
+  float mu0 = 0.f, mu1 = 0.f;                // m with -inf read as 0
+  float th0 = -INFINITY, th1 = -INFINITY;    // (m + slack) in raw score units
+  const float sl2 = args.scale_log2;         // > 0
   const int key_base = warp * 16;
   bool ok = true;
 
@@ -289,18 +291,32 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
     // ---- online softmax (log2 domain) with a lazily raised reference max:
     // m0/m1 only move when a score exceeds them by more than kRescaleSlack,
     // so exponentials stay below 2^kRescaleSlack and the O rescale is rare.
-    float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1])) * sl2;
-    float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3])) * sl2;
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const bool grow0 = mx0 > m0 + kRescaleSlack, grow1 = mx1 > m1 + kRescaleSlack;
-    if (__any_sync(0xffffffffu, grow0 || grow1)) {
+    // Most pages raise nothing: each thread tests its own raw scores against
+    // the rows' thresholds, and only a page on which some score passes one
+    // pays for the quad max (a row's scores sit in four lanes) and the
+    // rescale.  (Near a threshold the raw test and the scaled one may
+    // disagree; either way the exponentials stay far from overflow.)
+    const float rx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+    const float rx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+    if (__any_sync(0xffffffffu, rx0 > th0 || rx1 > th1)) {
+      float mx0 = rx0 * sl2, mx1 = rx1 * sl2;
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const bool grow0 = mx0 > m0 + kRescaleSlack, grow1 = mx1 > m1 + kRescaleSlack;
       const float a0 = grow0 ? ex2(m0 - mx0) : 1.f;
       const float a1 = grow1 ? ex2(m1 - mx1) : 1.f;
-      if (grow0) m0 = mx0;
-      if (grow1) m1 = mx1;
+      if (grow0) {
+        m0 = mx0;
+        mu0 = m0;
+        th0 = (m0 + kRescaleSlack) / sl2;
+      }
+      if (grow1) {
+        m1 = mx1;
+        mu1 = m1;
+        th1 = (m1 + kRescaleSlack) / sl2;
+      }
       l0 *= a0;
       l1 *= a1;
 #pragma unroll
@@ -311,8 +327,6 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
         o[j][3] *= a1;
       }
     }
-    const float mu0 = m0 == -INFINITY ? 0.f : m0;
-    const float mu1 = m1 == -INFINITY ? 0.f : m1;
     float p[2][4];
 #pragma unroll
     for (int n = 0; n < 2; ++n) {
@@ -370,16 +384,16 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
     mt0 = fmaxf(mt0, sm->m_part[w][r0]);
     mt1 = fmaxf(mt1, sm->m_part[w][r1]);
   }
-  const float mu0 = mt0 == -INFINITY ? 0.f : mt0;
-  const float mu1 = mt1 == -INFINITY ? 0.f : mt1;
+  const float mv0 = mt0 == -INFINITY ? 0.f : mt0;
+  const float mv1 = mt1 == -INFINITY ? 0.f : mt1;
   float lt0 = 0.f, lt1 = 0.f;
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
-    lt0 += sm->l_part[w][r0] * ex2(sm->m_part[w][r0] - mu0);
-    lt1 += sm->l_part[w][r1] * ex2(sm->m_part[w][r1] - mu1);
+    lt0 += sm->l_part[w][r0] * ex2(sm->m_part[w][r0] - mv0);
+    lt1 += sm->l_part[w][r1] * ex2(sm->m_part[w][r1] - mv1);
   }
-  const float f0 = (lt0 > 0.f ? ex2(m0 - mu0) / lt0 : 0.f);
-  const float f1 = (lt1 > 0.f ? ex2(m1 - mu1) / lt1 : 0.f);
+  const float f0 = (lt0 > 0.f ? ex2(m0 - mv0) / lt0 : 0.f);
+  const float f1 = (lt1 > 0.f ? ex2(m1 - mv1) / lt1 : 0.f);
   // Stage memory is idle once every page was consumed: sum partial O there.
   float* acc = reinterpret_cast<float*>(stages);  // [4 warps][16 rows][128 dims]
   {
