@@ -334,7 +334,10 @@ def run_ours(args):
 
         # NCCL's initialisation log (one line set per rank and channel) shows
         # how many ranks joined and over which transport.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        # A level below INFO (some machines preset VERSION or WARN) is raised
+        # to INFO; an explicit INFO or TRACE is kept.
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION", "WARN"):
+            os.environ["NCCL_DEBUG"] = "INFO"
         os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
         runner = SequenceParallelRunner(shape, dev, seed=args.seed)
@@ -391,7 +394,8 @@ def run_ours(args):
     value = n / (ms_step / 1e3)
     e2e_s = e2e_total / args.steps
 
-    stage = {"compress": [], "select": [], "attn": []}
+    # "gather": the visible part of the K/V all-gather (sequence-parallel only).
+    stage = {"compress": [], "select": [], "attn": [], "gather": []}
     for name, a, b in timers:
         stage[name].append(a.elapsed_time(b))
 
@@ -432,6 +436,7 @@ def run_ours(args):
         "config": workload_config(n, args.layers, world),
         "select_attn_ms_per_layer": stage_ms["select"] + attn_ms + stage_ms["compress"],
         "stage_ms_per_layer": stage_ms,
+        "kv_gather_ms_per_layer": stage_ms.get("gather"),
         "e2e": {"value": n / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": n * 8,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_layer * layers * args.steps,
@@ -445,8 +450,10 @@ def run_ours(args):
             "peak_kind": f"{pk_kind} (bf16 dense, sustained)",
             "flops_per_layer": flops_per_layer,
             "attn_launches_per_layer": chunks,
-            "traffic": ATTN_TRAFFIC_BYTES,
-            "traffic_source": ATTN_TRAFFIC_SOURCE,
+            # The capture is of one single-GPU 128K launch; a rank's chunk
+            # launches are smaller, so no per-launch figure is claimed there.
+            "traffic": ATTN_TRAFFIC_BYTES if world == 1 else None,
+            "traffic_source": ATTN_TRAFFIC_SOURCE if world == 1 else None,
         },
         "clocks": clocks.summary(),
     }

@@ -363,7 +363,7 @@ class SequenceParallelRunner:
             del attn
             m.mlp_residual(layer, h)
         if timers is not None:
-            timers.extend(t for t in layer_timers if t[0] != "gather")
+            timers.extend(layer_timers)
         if self.rank == 0:
             return m.logits(h[-1:])
         return None
