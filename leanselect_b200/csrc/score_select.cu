@@ -510,7 +510,7 @@ constexpr int kKeptCap = 512;              // candidates kept above the estimate
 
 struct TopkWarpSmem {
   uint4 row[kRowChunks];        // the row's candidate scores (bf16), 16-byte aligned copy
-  uint32_t hist[256];           // radix / sample histograms
+  uint32_t hist[256];           // radix histogram
   uint32_t kept[kKeptCap];      // candidates at or above the cut, in candidate order:
                                 // key << 16 | candidate index
 };
@@ -619,9 +619,9 @@ __device__ int compact_ge(const Src& src, int off, int m, __nv_bfloat162 cut, co
 // ascending order.  Returns the next output position.
 //
 // Candidates at or above a cut estimated from a 1/8 sample (every 8th
-// round of chunks; a 128-bin histogram linear in value between the sample's
-// min and max, aiming at ~2.5x the needed count) go to the warp's kept
-// buffer in one pass; the exact radix select then runs over those.  When
+// round of chunks; the normal quantile at the sample's mean and spread,
+// aiming at ~2.5x the needed count) go to the warp's kept buffer in one
+// pass; the exact radix select then runs over those.  When
 // the estimate kept too few or too many, the exact radix runs over the
 // whole row, read from the workspace (`row`).  `release()` is called once
 // `src` will not be read again (its shared-memory copy may then be reused).
@@ -641,10 +641,11 @@ __device__ int select_row(const Src& src, const GlobalChunks& row, int off, int 
     release();
     return k_out;
   }
-  // ---- 1/8 sample: value range and count of the finite sampled scores.
+  // ---- 1/8 sample (the first 256 candidates of every 2048): how many were
+  // sampled, and the mean and spread of the finite ones.
   const int nch = (off + m + 7) >> 3;
-  float smin = INFINITY, smax = -INFINITY;
-  int sampled = 0;
+  float s1 = 0.f, s2 = 0.f;
+  int sampled = 0, finite_s = 0;
   for (int base = 0; base < nch; base += 256) {
     const int c = base + lane;
     if (c < nch) {
@@ -656,10 +657,10 @@ __device__ int select_row(const Src& src, const GlobalChunks& row, int off, int 
         if (full || (first + e >= 0 && first + e < m)) {
           ++sampled;
           const float x = bf16_value(chunk_bits(v, e));
-          // fminf / fmaxf drop NaN; infinities are left out of the range.
-          if (fabsf(x) < INFINITY) {
-            smin = fminf(smin, x);
-            smax = fmaxf(smax, x);
+          if (fabsf(x) < INFINITY) {  // NaN and infinities are left out
+            ++finite_s;
+            s1 += x;
+            s2 = fmaf(x, x, s2);
           }
         }
       }
@@ -668,71 +669,25 @@ __device__ int select_row(const Src& src, const GlobalChunks& row, int off, int 
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     sampled += __shfl_xor_sync(0xffffffffu, sampled, o);
-    smin = fminf(smin, __shfl_xor_sync(0xffffffffu, smin, o));
-    smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
+    finite_s += __shfl_xor_sync(0xffffffffu, finite_s, o);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
   }
-  // The cut: the lower edge of the bin of a 128-bin histogram, linear in
-  // value between the sample's min and max, where the count from the top
-  // reaches ~1.5 cap * sampled / m.  -inf keeps every finite candidate.
+  // The cut: the normal quantile, at the sample's mean and spread, above
+  // which ~2.5x the needed count of candidates lies.  It is only an
+  // estimate: whatever it keeps is searched exactly below, and a row where it
+  // kept too few (< cap) or too many (> kKeptCap) is searched whole.  On the
+  // benchmark's synthetic rows it keeps 1.1x - 2.7x of cap (1st - 99th
+  // percentile), and no row of a 128K-token layer is searched whole.
   float cut = -INFINITY;
-  if (smax > smin) {
-    const float scale = 128.f / (smax - smin);
-    uint32_t* hist = ws->hist;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) hist[lane + 32 * j] = 0;
-    __syncwarp();
-    for (int base = 0; base < nch; base += 256) {
-      const int c = base + lane;
-      if (c < nch) {
-        const uint4 v = src.chunk(c);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int i = 8 * c + e - off;
-          const float x = bf16_value(chunk_bits(v, e));
-          if (i >= 0 && i < m && x > -INFINITY && x < INFINITY)
-            atomicAdd(&hist[min(127, static_cast<int>((x - smin) * scale))], 1u);
-        }
-      }
+  if (finite_s > 1) {
+    const float keep = 2.5f * static_cast<float>(cap) * static_cast<float>(sampled) /
+                       (static_cast<float>(m) * static_cast<float>(finite_s));
+    if (keep < 1.f) {
+      const float mean = s1 / static_cast<float>(finite_s);
+      const float var = fmaxf(0.f, s2 / static_cast<float>(finite_s) - mean * mean);
+      cut = mean + normcdfinvf(1.f - keep) * sqrtf(var);
     }
-    __syncwarp();
-    // ~2.5x the needed count: the kept count then falls short of cap (and
-    // the whole row is searched) for well under 1% of rows.
-    const int target = max(1, min(sampled, static_cast<int>(2.5f * cap * sampled / m) + 2));
-    uint32_t c4[4];
-    uint32_t lane_sum = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      c4[j] = hist[127 - 4 * lane - j];
-      lane_sum += c4[j];
-    }
-    uint32_t incl = lane_sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
-    }
-    const uint32_t excl = incl - lane_sum;
-    const bool here = excl < static_cast<uint32_t>(target) && incl >= static_cast<uint32_t>(target);
-    const uint32_t owner_mask = __ballot_sync(0xffffffffu, here);
-    int bin = 0;
-    if (here) {
-      uint32_t cum = excl;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        cum += c4[j];
-        if (cum >= static_cast<uint32_t>(target)) {
-          bin = 127 - 4 * lane - j;
-          break;
-        }
-      }
-    }
-    if (owner_mask != 0u) {
-      bin = __shfl_sync(0xffffffffu, bin, __ffs(owner_mask) - 1);
-      // A candidate of bin b >= bin has (x - smin) * scale >= bin, so x is at
-      // least this edge up to one rounding; stepping one ulp down keeps it.
-      cut = bin > 0 ? nextafterf(smin + static_cast<float>(bin) / scale, -INFINITY) : -INFINITY;
-    }
-    __syncwarp();
   }
   // ---- one pass: keep the candidates at or above the cut, in candidate order.
   // A bf16 score is >= cut iff it is >= cut rounded up to bf16.
