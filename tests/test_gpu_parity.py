@@ -321,6 +321,44 @@ def test_topk_exact_on_gpu_page_scores(case):
     assert ops.check_status(DEV) == 0
 
 
+@pytest.mark.parametrize("shape", ["few_above_a_tie", "nearly_all_tied"])
+def test_topk_exact_when_the_cut_estimate_misses(shape):
+    """Score distributions that defeat the top-k's sampled cut.  Every query
+    row is the same, and each atom key is a multiple alpha of one direction,
+    so a page scores the largest alpha of its five atoms.  "few_above_a_tie":
+    alpha = 0 (an exact tie) except 1.5 % of atoms far above it, so the cut
+    keeps fewer pages than the budget; "nearly_all_tied": alpha = 1 for 60 %
+    of atoms, so almost every page ties at the top and rows of more than 512
+    candidates keep too many.  Those rows are searched whole (on the CPU the
+    estimate misses on 332 and 164 of the sampled rows); the result must
+    still be the exact top-k of the GPU's page scores, ties to the lower
+    page."""
+    from measure.inputs import make_selector
+
+    n, take = 49152, 67
+    w = make_selector(DEV, 5).kernel_weights()
+    gen = torch.Generator().manual_seed(17)
+    q = torch.randn(1, 32, 128, generator=gen).expand(n, 32, 128).contiguous().to(DEV, torch.bfloat16)
+    atoms = (n - 32) // 16 + 1
+    if shape == "few_above_a_tie":
+        alpha = torch.zeros(atoms)
+        hot = torch.randperm(atoms, generator=gen)[: atoms * 3 // 200]
+        alpha[hot] = 8 + 4 * torch.rand(len(hot), generator=gen)
+    else:
+        alpha = torch.where(torch.rand(atoms, generator=gen) < 0.6, torch.ones(atoms),
+                            -2 + 2.99 * torch.rand(atoms, generator=gen))
+    qs = ops.project_queries(q[:1], w.wq_t, 2).float()[:, 0, :]        # [G, F]
+    u = qs / qs.pow(2).sum(-1, keepdim=True)                             # qs . u = 1
+    ks = (alpha.to(DEV)[None, :, None] * u[:, None, :]).to(torch.bfloat16).contiguous()
+    cq, cc = cu_dev([0, n]), cu_dev([0, atoms])
+    got = ops.select_pages(q, w, ks, cq, cc, n, take=take).cpu().numpy()
+    pages = ops.score_pages(q, w, ks, cq, cc, n).cpu().numpy()
+    rows = np.r_[np.arange(0, n, 97), np.arange(n - 64, n)]
+    want = ora.select_from_scores(pages[:, rows], rows, take=take)
+    np.testing.assert_array_equal(got[:, rows], want.topk_idx)
+    assert ops.check_status(DEV) == 0
+
+
 @pytest.mark.parametrize("name", ["stock_8k", "stock_ragged", "bench_16k"])
 def test_selection_matches_reference_fixture(name):
     """GPU selection against the reference's own ``topk_idx`` (tests/golden,
