@@ -51,6 +51,9 @@ extern "C" {
 /* Largest per-row page budget T accepted by ls_select_pages/ls_sparse_attn. */
 #define LS_MAX_TOPK 128
 
+/* Most page-list slices per row accepted by ls_sparse_attn_split. */
+#define LS_MAX_ATTN_SPLITS 64
+
 /* Human-readable name of an LS_ERR_* code. */
 const char* ls_status_string(int code);
 
@@ -356,6 +359,29 @@ int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                    const int32_t* topk_idx, int32_t topk, int32_t block_size,
                    float softmax_scale, int32_t causal, uint16_t* out, float* lse,
                    int32_t* status, void* stream);
+
+/*
+ * ls_sparse_attn_split -- ls_sparse_attn for few query rows, such as a decode
+ * step (the same infllmv2_attn_varlen_func call with max_seqlen_q == 1 and
+ * causal == 0, minicpm.py:3229-3243).  One CTA per (token, group) leaves
+ * most of the GPU idle when there are few tokens; here each row's sorted,
+ * de-duplicated page list is cut into `splits` contiguous slices (1 ..
+ * LS_MAX_ATTN_SPLITS), one CTA each, and a second kernel combines the
+ * slices' partial softmax results (each slice's output weighted by its share
+ * of the row's exponential mass).  Same arguments and results as
+ * ls_sparse_attn up to fp32 summation order; `workspace` holds
+ * ls_sparse_attn_split_workspace_bytes(total_q, H, splits) bytes
+ * (16-byte aligned; unused when splits == 1).
+ */
+size_t ls_sparse_attn_split_workspace_bytes(int64_t total_q, int32_t num_heads, int32_t splits);
+int ls_sparse_attn_split(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                         const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t batch,
+                         int32_t max_seqlen_q, int32_t max_seqlen_k, int64_t total_q,
+                         int64_t total_k, int32_t num_heads, int32_t num_kv_heads,
+                         int32_t head_dim, const int32_t* topk_idx, int32_t topk,
+                         int32_t block_size, float softmax_scale, int32_t causal, int32_t splits,
+                         void* workspace, size_t workspace_bytes, uint16_t* out, float* lse,
+                         int32_t* status, void* stream);
 
 /*
  * ls_sparse_attn_gather_only -- measurement twin of ls_sparse_attn (no

@@ -23,6 +23,7 @@ LS_DEVERR_PAGE_INDEX = 0x2
 LS_DEVERR_SEQLENS = 0x4
 
 LS_MAX_TOPK = 128
+LS_MAX_ATTN_SPLITS = 64
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -61,6 +62,8 @@ SIGNATURES = {
     "ls_bb_silu_mul": [_P, _I64, _I32, _P, _P],
     "ls_sparse_attn": [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _P,
                        _I32, _I32, _F32, _I32, _P, _P, _P, _P],
+    "ls_sparse_attn_split": [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I32, _I32, _I32,
+                             _P, _I32, _I32, _F32, _I32, _I32, _P, _SZ, _P, _P, _P, _P],
     "ls_sparse_attn_gather_only": [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I32, _I32,
                                    _I32, _P, _I32, _I32, _I32, _P, _P],
     "ls_wait_timeout_probe": [_P, _P, ctypes.c_uint64, _P],
@@ -68,7 +71,8 @@ SIGNATURES = {
 STRING_FUNCS = ("ls_status_string", "ls_last_error", "ls_version")
 SIZE_FUNCS = {"ls_select_pages_workspace_bytes": [_I64, _I32, _I32],
               "ls_select_pages_f32_workspace_bytes": [_I64, _I64, _I32, _I32],
-              "ls_uniform_select_workspace_bytes": [_I64, _I64, _I32, _I32, _I32]}
+              "ls_uniform_select_workspace_bytes": [_I64, _I64, _I32, _I32, _I32],
+              "ls_sparse_attn_split_workspace_bytes": [_I64, _I32, _I32]}
 
 _lock = threading.Lock()
 _lib = None

@@ -583,9 +583,11 @@ int sparse_attn_impl(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                      int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
                      const int32_t* topk_idx, int32_t topk, int32_t block_size,
                      float softmax_scale, int32_t causal, uint16_t* out, float* lse,
-                     int32_t* status, void* stream, bool gather_only) {
+                     int32_t* status, void* stream, bool gather_only, int32_t splits = 1,
+                     void* workspace = nullptr, size_t workspace_bytes = 0) {
   LS_REQUIRE(q && k && v && cu_seqlens_q && cu_seqlens_k && (out || gather_only),
              "null argument");
+  LS_REQUIRE(splits >= 1 && splits <= LS_MAX_ATTN_SPLITS, "splits must lie in [1, 64]");
   LS_REQUIRE(batch >= 1 && total_q >= 0 && total_k >= 0, "bad sizes");
   LS_REQUIRE(total_q < (int64_t{1} << 31) && total_k < (int64_t{1} << 31), "totals out of range");
   LS_REQUIRE(max_seqlen_q >= 0 && max_seqlen_k >= 0, "bad max_seqlen");
@@ -603,7 +605,18 @@ int sparse_attn_impl(const uint16_t* q, const uint16_t* k, const uint16_t* v,
   LS_REQUIRE_ALIGNED(v);
   if (out) LS_REQUIRE_ALIGNED(out);
   if (total_q == 0) return LS_OK;
+  LS_REQUIRE(total_q * num_kv_heads * splits < (int64_t{1} << 31), "too many CTAs");
   AttnArgs a{};
+  a.splits = splits;
+  if (splits > 1) {
+    const size_t need = ls_sparse_attn_split_workspace_bytes(total_q, num_heads, splits);
+    LS_REQUIRE(workspace, "null workspace");
+    LS_REQUIRE_ALIGNED(workspace);
+    LS_REQUIRE(workspace_bytes >= need, "workspace too small");
+    const int64_t rows = total_q * num_heads;
+    a.part_o = static_cast<float*>(workspace);
+    a.part_ml = a.part_o + static_cast<int64_t>(splits) * rows * 128;
+  }
   const uint64_t row = static_cast<uint64_t>(num_kv_heads) * 128;
   const uint64_t rows = static_cast<uint64_t>(std::max<int64_t>(total_k, 1));
   if (!make_tensor_map_2d(&a.tm_k, k, rows, row, row * 2, 64, 64))
@@ -628,9 +641,11 @@ int sparse_attn_impl(const uint16_t* q, const uint16_t* k, const uint16_t* v,
   a.lse = lse;
   a.status = status;
   a.order = 1;  // group-major: resident CTAs share one group's K/V in L2
-  const cudaError_t err = gather_only
-                              ? launch_sparse_attn_gather_only(a, static_cast<cudaStream_t>(stream))
-                              : launch_sparse_attn(a, static_cast<cudaStream_t>(stream));
+  cudaError_t err = gather_only
+                        ? launch_sparse_attn_gather_only(a, static_cast<cudaStream_t>(stream))
+                        : launch_sparse_attn(a, static_cast<cudaStream_t>(stream));
+  if (err == cudaSuccess && !gather_only && splits > 1)
+    err = launch_sparse_attn_merge(a, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? LS_OK : cuda_fail(err, "sparse_attn launch");
 }
 
@@ -646,6 +661,26 @@ int ls_sparse_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v,
   return sparse_attn_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, batch, max_seqlen_q, max_seqlen_k,
                           total_q, total_k, num_heads, num_kv_heads, head_dim, topk_idx, topk,
                           block_size, softmax_scale, causal, out, lse, status, stream, false);
+}
+
+size_t ls_sparse_attn_split_workspace_bytes(int64_t total_q, int32_t num_heads, int32_t splits) {
+  if (total_q <= 0 || num_heads <= 0 || splits <= 1) return 0;
+  return static_cast<size_t>(splits) * static_cast<size_t>(total_q) *
+         static_cast<size_t>(num_heads) * (128 + 2) * sizeof(float);
+}
+
+int ls_sparse_attn_split(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                         const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t batch,
+                         int32_t max_seqlen_q, int32_t max_seqlen_k, int64_t total_q,
+                         int64_t total_k, int32_t num_heads, int32_t num_kv_heads,
+                         int32_t head_dim, const int32_t* topk_idx, int32_t topk,
+                         int32_t block_size, float softmax_scale, int32_t causal, int32_t splits,
+                         void* workspace, size_t workspace_bytes, uint16_t* out, float* lse,
+                         int32_t* status, void* stream) {
+  return sparse_attn_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, batch, max_seqlen_q, max_seqlen_k,
+                          total_q, total_k, num_heads, num_kv_heads, head_dim, topk_idx, topk,
+                          block_size, softmax_scale, causal, out, lse, status, stream, false,
+                          splits, workspace, workspace_bytes);
 }
 
 int ls_wait_timeout_probe(int32_t* status, int32_t* done, uint64_t timeout_ns, void* stream) {

@@ -104,9 +104,21 @@ struct AttnArgs {
   float* lse;
   int32_t* status;
   int order;           // CTA order: 0 token-major (groups interleaved), 1 group-major
+  // Split pages (decode): each (token, group) row's sorted page list is cut
+  // into `splits` contiguous slices, one CTA each; the CTAs write normalised
+  // partial outputs and (row max in log2 units, row sum), which
+  // launch_sparse_attn_merge combines.  splits == 1: no workspace, the CTA
+  // writes `out` (and `lse`) itself.
+  int splits;
+  float* part_o;       // [splits, total_q * num_heads, 128]
+  float* part_ml;      // [splits, total_q * num_heads, 2]
 };
 
 cudaError_t launch_sparse_attn(const AttnArgs& args, cudaStream_t stream);
+
+// Combines the split partial results of a launch_sparse_attn with
+// args.splits > 1 into `out` (and `lse`).
+cudaError_t launch_sparse_attn_merge(const AttnArgs& args, cudaStream_t stream);
 
 // The attention launch's data movement alone: same grid, page lists, TMA
 // boxes and shared-memory ring, consumers release each stage unread and

@@ -244,81 +244,103 @@ cudaError_t launch_compressed_seqlens(const int32_t* cu_k, int batch, int kernel
 // with kernel 128 / stride 64)
 // ---------------------------------------------------------------------------
 //
-// One thread per (sequence, 64-key block b, 16-byte vector).  It sums the
-// 16-key runs 4b .. 4b+7 of its vector (each sequentially in fp32) and
-// writes the 32/16 atoms 4b .. 4b+3 (runs a and a+1 added) and the 128/64
-// atom b (runs 4b .. 4b+7 added in order), scaled and rounded to bf16: the
-// order of compress_keys_kernel for both geometries, so either compressor
-// gives the same bits.  Each key is read by two neighbouring blocks (the
-// second read hits L2), where two separate compressions read it four times.
+// A CTA takes 8 consecutive 64-key blocks of one sequence and 16 of the
+// 16-byte vectors of a key row (256 bytes).  Phase 1: every thread sums
+// 16-key runs of one vector (each run sequentially in fp32, 16 loads in
+// flight), the 32 runs of the CTA's blocks plus the next block's first 4,
+// into shared memory.  Phase 2: the 32/16 atom a is runs a and a+1 added,
+// the 128/64 atom b is runs 4b .. 4b+7 added in order, both scaled and
+// rounded to bf16 -- the order of compress_keys_kernel for both geometries,
+// so either compressor gives the same bits.  K is read 1.125 times, where
+// two separate compressions read it three times.
+constexpr int kDualBlocks = 8;                   // 64-key blocks per CTA
+constexpr int kDualVecs = 16;                    // 16-byte vectors per CTA
+constexpr int kDualRuns = 4 * kDualBlocks + 4;   // + the next block's first 4 runs
 
 __global__ void __launch_bounds__(256) compress_keys_dual_kernel(
     const uint4* __restrict__ k, const int32_t* __restrict__ cu_k, const int32_t* __restrict__ cu_c,
     const int32_t* __restrict__ cu_c2, int64_t total_k, int vecs_per_row,
     uint4* __restrict__ kc, uint4* __restrict__ kc2, int32_t* status) {
+  __shared__ float4 runs[kDualRuns][kDualVecs][2];  // 18 KB: 8 fp32 sums per (run, vector)
   const int b = blockIdx.y;
-  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int blk = static_cast<int>(gid / vecs_per_row);
-  const int vec = static_cast<int>(gid % vecs_per_row);
+  const int blk0 = static_cast<int>(blockIdx.x) * kDualBlocks;
+  const int vec0 = static_cast<int>(blockIdx.z) * kDualVecs;
+  const int64_t k0 = __ldg(cu_k + b), k1 = __ldg(cu_k + b + 1);
   const int64_t c0 = __ldg(cu_c + b), c20 = __ldg(cu_c2 + b);
   const int atoms = static_cast<int>(__ldg(cu_c + b + 1) - c0);
   const int atoms2 = static_cast<int>(__ldg(cu_c2 + b + 1) - c20);
   // A 128/64 atom b needs keys [64b, 64b+128), so it implies the 32/16 atom 4b.
-  if (4 * blk >= atoms) return;
-  const bool has2 = blk < atoms2;
-  const int first = 4 * blk;
-  const int last = has2 ? first + 7 : min(first + 4, atoms);  // last run read
-  const int64_t tok0 = __ldg(cu_k + b) + static_cast<int64_t>(first) * 16;
-  if (tok0 + static_cast<int64_t>(last - first + 1) * 16 > total_k) {
-    report(status, LS_DEVERR_SEQLENS);
+  if (4 * blk0 >= atoms) return;
+  if (k1 > total_k || k1 < k0) {
+    if (threadIdx.x == 0) report(status, LS_DEVERR_SEQLENS);
     return;
   }
-  const uint4* src = k + tok0 * vecs_per_row + vec;
-  float prev[8], acc2[8];
-#pragma unroll
-  for (int c = 0; c < 8; ++c) prev[c] = acc2[c] = 0.f;
-  for (int j = first; j <= last; ++j) {
+  const int64_t n_runs = (k1 - k0) / 16;  // complete 16-key runs of the sequence
+  const int r0 = 4 * blk0;
+  for (int item = threadIdx.x; item < kDualRuns * kDualVecs; item += blockDim.x) {
+    const int rr = item / kDualVecs, v = item % kDualVecs;
     float run[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) run[c] = 0.f;
-    const uint4* rs = src + static_cast<int64_t>(j - first) * 16 * vecs_per_row;
-#pragma unroll 4
-    for (int t = 0; t < 16; ++t) {
-      const uint4 u = __ldg(rs + static_cast<int64_t>(t) * vecs_per_row);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    if (r0 + rr < n_runs && vec0 + v < vecs_per_row) {
+      const uint4* src = k + (k0 + 16 * static_cast<int64_t>(r0 + rr)) * vecs_per_row + vec0 + v;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float2 f = __bfloat1622float2(h[c]);
-        run[2 * c] += f.x;
-        run[2 * c + 1] += f.y;
+      for (int t = 0; t < 16; ++t) {
+        const uint4 u = __ldg(src + static_cast<int64_t>(t) * vecs_per_row);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float2 f = __bfloat1622float2(h[c]);
+          run[2 * c] += f.x;
+          run[2 * c + 1] += f.y;
+        }
       }
     }
-    const int a = j - 1;  // the 32/16 atom that ends with this run
-    if (j > first && a < atoms && a <= first + 3) {
-      float acc[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) acc[c] = (0.f + prev[c]) + run[c];
-      uint4 out;
-      out.x = pack_bf16x2(acc[0] * (1.f / 32.f), acc[1] * (1.f / 32.f));
-      out.y = pack_bf16x2(acc[2] * (1.f / 32.f), acc[3] * (1.f / 32.f));
-      out.z = pack_bf16x2(acc[4] * (1.f / 32.f), acc[5] * (1.f / 32.f));
-      out.w = pack_bf16x2(acc[6] * (1.f / 32.f), acc[7] * (1.f / 32.f));
-      kc[(c0 + a) * vecs_per_row + vec] = out;
-    }
-    if (has2) {
-#pragma unroll
-      for (int c = 0; c < 8; ++c) acc2[c] += run[c];
-    }
-#pragma unroll
-    for (int c = 0; c < 8; ++c) prev[c] = run[c];
+    runs[rr][v][0] = make_float4(run[0], run[1], run[2], run[3]);
+    runs[rr][v][1] = make_float4(run[4], run[5], run[6], run[7]);
   }
-  if (has2) {
+  __syncthreads();
+  // 32/16 atoms r0 + i: runs i and i + 1.
+  for (int item = threadIdx.x; item < 4 * kDualBlocks * kDualVecs; item += blockDim.x) {
+    const int i = item / kDualVecs, v = item % kDualVecs;
+    const int a = r0 + i;
+    if (a >= atoms || vec0 + v >= vecs_per_row) continue;
+    const float4 p0 = runs[i][v][0], p1 = runs[i][v][1];
+    const float4 n0 = runs[i + 1][v][0], n1 = runs[i + 1][v][1];
+    const float s = 1.f / 32.f;
     uint4 out;
-    out.x = pack_bf16x2(acc2[0] * (1.f / 128.f), acc2[1] * (1.f / 128.f));
-    out.y = pack_bf16x2(acc2[2] * (1.f / 128.f), acc2[3] * (1.f / 128.f));
-    out.z = pack_bf16x2(acc2[4] * (1.f / 128.f), acc2[5] * (1.f / 128.f));
-    out.w = pack_bf16x2(acc2[6] * (1.f / 128.f), acc2[7] * (1.f / 128.f));
-    kc2[(c20 + blk) * vecs_per_row + vec] = out;
+    out.x = pack_bf16x2(((0.f + p0.x) + n0.x) * s, ((0.f + p0.y) + n0.y) * s);
+    out.y = pack_bf16x2(((0.f + p0.z) + n0.z) * s, ((0.f + p0.w) + n0.w) * s);
+    out.z = pack_bf16x2(((0.f + p1.x) + n1.x) * s, ((0.f + p1.y) + n1.y) * s);
+    out.w = pack_bf16x2(((0.f + p1.z) + n1.z) * s, ((0.f + p1.w) + n1.w) * s);
+    kc[(c0 + a) * vecs_per_row + vec0 + v] = out;
+  }
+  // 128/64 atoms blk0 + j: runs 4j .. 4j + 7 in order.
+  for (int item = threadIdx.x; item < kDualBlocks * kDualVecs; item += blockDim.x) {
+    const int j = item / kDualVecs, v = item % kDualVecs;
+    if (blk0 + j >= atoms2 || vec0 + v >= vecs_per_row) continue;
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 x0 = runs[4 * j + q][v][0], x1 = runs[4 * j + q][v][1];
+      acc[0] += x0.x;
+      acc[1] += x0.y;
+      acc[2] += x0.z;
+      acc[3] += x0.w;
+      acc[4] += x1.x;
+      acc[5] += x1.y;
+      acc[6] += x1.z;
+      acc[7] += x1.w;
+    }
+    const float s = 1.f / 128.f;
+    uint4 out;
+    out.x = pack_bf16x2(acc[0] * s, acc[1] * s);
+    out.y = pack_bf16x2(acc[2] * s, acc[3] * s);
+    out.z = pack_bf16x2(acc[4] * s, acc[5] * s);
+    out.w = pack_bf16x2(acc[6] * s, acc[7] * s);
+    kc2[(c20 + blk0 + j) * vecs_per_row + vec0 + v] = out;
   }
 }
 
@@ -328,8 +350,10 @@ cudaError_t launch_compress_keys_dual(const uint16_t* k, const int32_t* cu_k, co
                                       int32_t* status, cudaStream_t stream) {
   if (max_atoms <= 0) return cudaSuccess;
   const int vecs = G * D / 8;
-  const int64_t threads = static_cast<int64_t>((max_atoms + 3) / 4) * vecs;
-  const dim3 grid(static_cast<unsigned>((threads + 255) / 256), static_cast<unsigned>(batch));
+  const int blocks64 = (max_atoms + 3) / 4;
+  const dim3 grid(static_cast<unsigned>((blocks64 + kDualBlocks - 1) / kDualBlocks),
+                  static_cast<unsigned>(batch),
+                  static_cast<unsigned>((vecs + kDualVecs - 1) / kDualVecs));
   compress_keys_dual_kernel<<<grid, 256, 0, stream>>>(
       reinterpret_cast<const uint4*>(k), cu_k, cu_c, cu_c2, total_k, vecs,
       reinterpret_cast<uint4*>(kc), reinterpret_cast<uint4*>(kc2), status);

@@ -366,25 +366,38 @@ __global__ void __launch_bounds__(kThreads, 2) score_kernel(const __grid_constan
               if (16 * (a_base + i) > pos) v[i] = -INFINITY;
           }
           if constexpr (MODE == kModeAtoms) {
-            // Raw atom scores, rounded to bf16 (the reference's bf16 einsum output).
-            if (valid && a_base < args.max_atoms) {
-              if ((args.max_atoms & 7) == 0) {
+            // Raw atom scores, rounded to bf16 (the reference's bf16 einsum
+            // output).  Rows lie max_atoms elements apart, of any parity, so
+            // each half of the warp's 32 rows x 32 atoms is staged in shared
+            // memory and written back as contiguous 32-byte row segments, two
+            // rows per store instruction (not 32 rows of 2 bytes).
+            uint16_t* st16 = reinterpret_cast<uint16_t*>(store_stage + quad * 256);
+            const int64_t row_base = static_cast<int64_t>(ti.g) * args.total_q + ti.q0 + ti.row0 +
+                                     quad * 32;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                  uint4 u;
-                  u.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
-                  u.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
-                  u.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
-                  u.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
-                  if (a_base + 8 * c < args.max_atoms)
-                    *reinterpret_cast<uint4*>(atom_row + a_base + 8 * c) = u;
-                }
-              } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  if (a_base + i < args.max_atoms)
-                    atom_row[a_base + i] = __bfloat16_as_ushort(__float2bfloat16_rn(v[i]));
+            for (int h = 0; h < 2; ++h) {
+              const int a0 = a_base + 16 * h;
+              if (a0 >= args.max_atoms) break;  // the same for the whole warp
+              uint4 u0, u1;
+              u0.x = pack_bf16x2(v[16 * h + 0], v[16 * h + 1]);
+              u0.y = pack_bf16x2(v[16 * h + 2], v[16 * h + 3]);
+              u0.z = pack_bf16x2(v[16 * h + 4], v[16 * h + 5]);
+              u0.w = pack_bf16x2(v[16 * h + 6], v[16 * h + 7]);
+              u1.x = pack_bf16x2(v[16 * h + 8], v[16 * h + 9]);
+              u1.y = pack_bf16x2(v[16 * h + 10], v[16 * h + 11]);
+              u1.z = pack_bf16x2(v[16 * h + 12], v[16 * h + 13]);
+              u1.w = pack_bf16x2(v[16 * h + 14], v[16 * h + 15]);
+              reinterpret_cast<uint4*>(st16 + lane * 16)[0] = u0;
+              reinterpret_cast<uint4*>(st16 + lane * 16)[1] = u1;
+              __syncwarp();
+              const int col = lane & 15;
+#pragma unroll 4
+              for (int rr = 0; rr < 32; rr += 2) {
+                const int r = rr + (lane >> 4);
+                if (quad * 32 + r < ti.rows && a0 + col < args.max_atoms)
+                  args.atom_out[(row_base + r) * args.max_atoms + a0 + col] = st16[r * 16 + col];
               }
+              __syncwarp();
             }
           } else {
             // Page p of this block pools atoms [4p-1, 4p+4): its first atom is

@@ -121,9 +121,13 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const bool group_major = args.order == 1;
-  const int64_t t = group_major ? blockIdx.x % args.total_q : blockIdx.x / args.num_groups;
-  const int g = group_major ? static_cast<int>(blockIdx.x / args.total_q)
-                            : static_cast<int>(blockIdx.x % args.num_groups);
+  // Slice `split` of the row's page list (the whole list when splits == 1);
+  // a row's slices are neighbouring CTAs.
+  const int split = static_cast<int>(blockIdx.x % static_cast<uint32_t>(args.splits));
+  const int64_t item = blockIdx.x / static_cast<uint32_t>(args.splits);
+  const int64_t t = group_major ? item % args.total_q : item / args.num_groups;
+  const int g = group_major ? static_cast<int>(item / args.total_q)
+                            : static_cast<int>(item % args.num_groups);
   const int b = find_sequence(args.cu_q, args.batch, t);
   const int64_t q_start = __ldg(args.cu_q + b);
   const int64_t k_start = __ldg(args.cu_k + b);
@@ -179,7 +183,10 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
     }
   }
   __syncthreads();
-  const int n_pages = sm->n_pages;
+  const int page_lo = static_cast<int>(static_cast<int64_t>(split) * sm->n_pages / args.splits);
+  const int n_pages =
+      static_cast<int>(static_cast<int64_t>(split + 1) * sm->n_pages / args.splits) - page_lo;
+  const int32_t* pages = sm->pages + page_lo;
   volatile int* abort_flag = &sm->abort_flag;
 
   if (warp == 4) {
@@ -194,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
         ok = mbar_wait(&sm->empty[s], ((i / kStages) & 1) ^ 1, args.status, abort_flag);
         if (!ok) break;
         uint8_t* st = stages + s * kStageBytes;
-        const int32_t y = static_cast<int32_t>(k_start + static_cast<int64_t>(sm->pages[i]) * 64);
+        const int32_t y = static_cast<int32_t>(k_start + static_cast<int64_t>(pages[i]) * 64);
         const int32_t x = g * 128;
         mbar_arrive_expect_tx(&sm->full[s], kStageBytes);
         tma_load_2d(st, &args.tm_k, &sm->full[s], x, y);
@@ -278,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
         for (int e = 0; e < 4; ++e) sc[n][e] += sh[n][e];
     }
     // ---- causal / length mask (only pages that reach past t_lim)
-    const int page_key0 = sm->pages[i] * 64 + key_base;
+    const int page_key0 = pages[i] * 64 + key_base;
     if (page_key0 + 15 > t_lim) {
 #pragma unroll
       for (int n = 0; n < 2; ++n)
@@ -424,23 +431,35 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
           sum[c + 2] += x.z;
           sum[c + 3] += x.w;
         }
-      uint4 packed[2];
-      uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+      // Row max (log2 units) and row sum of this CTA's pages.
+      float mt = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) pw[c] = pack_bf16x2(sum[2 * c], sum[2 * c + 1]);
-      uint4* dst = reinterpret_cast<uint4*>(args.out + (t * args.num_heads + g * HG + row) * 128 + col0);
-      dst[0] = packed[0];
-      dst[1] = packed[1];
-      if (args.lse != nullptr && (threadIdx.x & 7) == 0) {
-        float mt = -INFINITY;
+      for (int w = 0; w < 4; ++w) mt = fmaxf(mt, sm->m_part[w][row]);
+      const float mu = mt == -INFINITY ? 0.f : mt;
+      float lt = 0.f;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) mt = fmaxf(mt, sm->m_part[w][row]);
-        const float mu = mt == -INFINITY ? 0.f : mt;
-        float lt = 0.f;
+      for (int w = 0; w < 4; ++w) lt += sm->l_part[w][row] * ex2(sm->m_part[w][row] - mu);
+      const int64_t orow = t * args.num_heads + g * HG + row;
+      if (args.splits > 1) {
+        // Partial result of this slice: normalised output, max and sum.
+        const int64_t prow = static_cast<int64_t>(split) * args.total_q * args.num_heads + orow;
+        float4* po = reinterpret_cast<float4*>(args.part_o + prow * 128 + col0);
 #pragma unroll
-        for (int w = 0; w < 4; ++w) lt += sm->l_part[w][row] * ex2(sm->m_part[w][row] - mu);
-        args.lse[static_cast<int64_t>(g * HG + row) * args.total_q + t] =
-            lt > 0.f ? (mt + __log2f(lt)) * 0.69314718055994531f : INFINITY;
+        for (int c = 0; c < 4; ++c)
+          po[c] = make_float4(sum[4 * c], sum[4 * c + 1], sum[4 * c + 2], sum[4 * c + 3]);
+        if ((threadIdx.x & 7) == 0)
+          *reinterpret_cast<float2*>(args.part_ml + prow * 2) = make_float2(mt, lt);
+      } else {
+        uint4 packed[2];
+        uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) pw[c] = pack_bf16x2(sum[2 * c], sum[2 * c + 1]);
+        uint4* dst = reinterpret_cast<uint4*>(args.out + orow * 128 + col0);
+        dst[0] = packed[0];
+        dst[1] = packed[1];
+        if (args.lse != nullptr && (threadIdx.x & 7) == 0)
+          args.lse[static_cast<int64_t>(g * HG + row) * args.total_q + t] =
+              lt > 0.f ? (mt + __log2f(lt)) * 0.69314718055994531f : INFINITY;
       }
     }
   }
@@ -448,11 +467,51 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
 
 size_t attn_smem_bytes() { return 1024 + kStages * kStageBytes + 16 * 256 + sizeof(AttnSmem); }
 
+// One warp per (token, head) row: weights each slice's normalised output by
+// its share of the row's softmax mass, l_s * 2^(m_s - max m), and writes the
+// bf16 row (zeros when no slice saw a page) and its log-sum-exp.
+__global__ void __launch_bounds__(256) attn_merge_kernel(const __grid_constant__ AttnArgs args) {
+  const int64_t rows = args.total_q * args.num_heads;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  float mx = -INFINITY;
+  for (int s = 0; s < args.splits; ++s) {
+    const float2 ml = *reinterpret_cast<const float2*>(args.part_ml + (s * rows + r) * 2);
+    if (ml.y > 0.f) mx = fmaxf(mx, ml.x);
+  }
+  float wsum = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < args.splits; ++s) {
+    const float2 ml = *reinterpret_cast<const float2*>(args.part_ml + (s * rows + r) * 2);
+    if (!(ml.y > 0.f)) continue;
+    const float w = ml.y * ex2(ml.x - mx);
+    const float4 o = reinterpret_cast<const float4*>(args.part_o + (s * rows + r) * 128)[lane];
+    wsum += w;
+    acc.x = fmaf(w, o.x, acc.x);
+    acc.y = fmaf(w, o.y, acc.y);
+    acc.z = fmaf(w, o.z, acc.z);
+    acc.w = fmaf(w, o.w, acc.w);
+  }
+  const float f = wsum > 0.f ? 1.f / wsum : 0.f;
+  uint2 packed;
+  packed.x = pack_bf16x2(acc.x * f, acc.y * f);
+  packed.y = pack_bf16x2(acc.z * f, acc.w * f);
+  reinterpret_cast<uint2*>(args.out + r * 128)[lane] = packed;
+  if (args.lse != nullptr && lane == 0) {
+    const int64_t t = r / args.num_heads;
+    const int h = static_cast<int>(r % args.num_heads);
+    args.lse[static_cast<int64_t>(h) * args.total_q + t] =
+        wsum > 0.f ? (mx + __log2f(wsum)) * 0.69314718055994531f : INFINITY;
+  }
+}
+
 }  // namespace
 
 template <bool kGatherOnly>
 cudaError_t launch_attn(const AttnArgs& args, cudaStream_t stream) {
-  const int64_t grid = args.total_q * args.num_groups;
+  if (args.splits < 1) return cudaErrorInvalidValue;
+  const int64_t grid = args.total_q * args.num_groups * args.splits;
   if (grid == 0) return cudaSuccess;
   const size_t smem = attn_smem_bytes();
   const int hg = args.num_heads / args.num_groups;
@@ -478,7 +537,16 @@ cudaError_t launch_sparse_attn(const AttnArgs& args, cudaStream_t stream) {
 }
 
 cudaError_t launch_sparse_attn_gather_only(const AttnArgs& args, cudaStream_t stream) {
-  return launch_attn<true>(args, stream);
+  AttnArgs a = args;
+  a.splits = 1;
+  return launch_attn<true>(a, stream);
+}
+
+cudaError_t launch_sparse_attn_merge(const AttnArgs& args, cudaStream_t stream) {
+  const int64_t rows = args.total_q * args.num_heads;
+  if (rows == 0) return cudaSuccess;
+  attn_merge_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(args);
+  return cudaGetLastError();
 }
 
 }  // namespace ls

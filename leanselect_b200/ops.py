@@ -17,7 +17,7 @@ from typing import Sequence
 import torch
 
 from . import _native
-from ._native import LS_MAX_TOPK, LeanSelectError
+from ._native import LS_MAX_ATTN_SPLITS, LS_MAX_TOPK, LeanSelectError
 
 _STATUS: dict[int, torch.Tensor] = {}
 
@@ -475,12 +475,37 @@ def select_pages_chunk(q: torch.Tensor, weights: FoldedWeights, ks: torch.Tensor
 # a9: sparse attention
 # ---------------------------------------------------------------------------
 
+def attn_splits(rows: int, max_seqlen_q: int, max_seqlen_k: int, topk: int,
+                device: torch.device) -> int:
+    """Page-list slices per row for :func:`sparse_attn` (1 = one CTA per row).
+
+    Only decode-shaped calls (one query per sequence) are split: with fewer
+    (token, group) rows than SMs, one CTA per row leaves SMs idle, so each
+    row's pages are cut into slices of at least 4 pages, up to about one CTA
+    per SM (more slices cost more in per-CTA set-up than they gain: measured
+    on 128K-token caches, batch 64 runs 70 us unsplit and 79 us in 3 slices).
+    Prefill keeps one CTA per row, so its results do not depend on how the
+    rows are batched.
+    """
+    if max_seqlen_q != 1 or rows <= 0:
+        return 1
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    pages = min(topk, -(-max(max_seqlen_k, 0) // 64))
+    want = sms // rows
+    return max(1, min(want, pages // 4, LS_MAX_ATTN_SPLITS))
+
+
 def sparse_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
                 cu_seqlens_k: torch.Tensor, max_seqlen_q: int, max_seqlen_k: int,
                 topk_idx: torch.Tensor, *, softmax_scale: float | None = None,
                 causal: bool = True, return_lse: bool = False, block_size: int = 64,
-                out: torch.Tensor | None = None):
-    """Block-sparse attention over per-token page lists (minicpm.py:3229-3243)."""
+                out: torch.Tensor | None = None, splits: int | None = None):
+    """Block-sparse attention over per-token page lists (minicpm.py:3229-3243).
+
+    ``splits`` cuts each row's page list into that many slices, one CTA each,
+    combined by a second kernel (``ls_sparse_attn_split``); ``None`` picks
+    it with :func:`attn_splits` (decode calls only).
+    """
     dev = _require_cuda(q, k, v, cu_seqlens_q, cu_seqlens_k, topk_idx)
     qb, kb, vb = _bf16(q), _bf16(k), _bf16(v)
     total_q, H, D = qb.shape
@@ -493,11 +518,22 @@ def sparse_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q:
     lse = torch.empty(H, total_q, dtype=torch.float32, device=dev) if return_lse else None
     cu_q, cu_k = _i32(cu_seqlens_q), _i32(cu_seqlens_k)
     scale = float(softmax_scale) if softmax_scale is not None else 1.0 / math.sqrt(D)
-    _call(dev, "ls_sparse_attn", qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), cu_q.data_ptr(),
-               cu_k.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q), int(max_seqlen_k),
-               total_q, total_k, H, G, D, idx.data_ptr(), idx.shape[2], block_size, scale,
-               1 if causal else 0, out.data_ptr(), _ptr(lse), status_word(dev).data_ptr(),
-               _stream(dev))
+    if splits is None:
+        splits = attn_splits(total_q * G, int(max_seqlen_q), int(max_seqlen_k), idx.shape[2], dev)
+    if splits > 1 and total_q:
+        nbytes = _native.load().ls_sparse_attn_split_workspace_bytes(total_q, H, int(splits))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        _call(dev, "ls_sparse_attn_split", qb.data_ptr(), kb.data_ptr(), vb.data_ptr(),
+              cu_q.data_ptr(), cu_k.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q),
+              int(max_seqlen_k), total_q, total_k, H, G, D, idx.data_ptr(), idx.shape[2],
+              block_size, scale, 1 if causal else 0, int(splits), ws.data_ptr(), nbytes,
+              out.data_ptr(), _ptr(lse), status_word(dev).data_ptr(), _stream(dev))
+    else:
+        _call(dev, "ls_sparse_attn", qb.data_ptr(), kb.data_ptr(), vb.data_ptr(),
+              cu_q.data_ptr(), cu_k.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q),
+              int(max_seqlen_k), total_q, total_k, H, G, D, idx.data_ptr(), idx.shape[2],
+              block_size, scale, 1 if causal else 0, out.data_ptr(), _ptr(lse),
+              status_word(dev).data_ptr(), _stream(dev))
     if q.dtype != torch.bfloat16:
         out = out.to(q.dtype)
     return (out, lse) if return_lse else out

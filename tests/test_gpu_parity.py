@@ -601,6 +601,71 @@ def test_decode_step_through_sparse_forward_contract():
     assert ops.check_status(DEV) == 0
 
 
+@pytest.mark.parametrize("splits", [None, 2, 7, 64])
+def test_decode_attention_with_split_page_lists(splits):
+    """Decode rows with their page lists cut into slices (``ls_sparse_attn_split``,
+    chosen automatically for decode calls): the slices' partial results,
+    combined by their share of each row's exponential mass, give the oracle's
+    attention and log-sum-exp, also when there are more slices than pages
+    (empty slices), for a row whose list is all -1 (zeros, lse +inf), and
+    within fp32 summation order of the one-CTA-per-row kernel."""
+    cache = [4096, 64, 777, 131, 2500]
+    heads, groups = 32, 2
+    inp = ora.synthetic_layer(cache, num_heads=heads, num_kv_heads=groups, head_dim=128,
+                              router_heads=4, router_dim=32, hot_pages=2, seed=83, bf16=True)
+    last = inp.cu_seqlens[1:] - 1
+    q = inp.q[last]
+    cu_q = np.arange(len(cache) + 1, dtype=np.int32)
+    rng = np.random.default_rng(11)
+    idx = np.full((groups, len(cache), 67), -1, dtype=np.int32)
+    for b, n in enumerate(cache):
+        pages = (n + 63) // 64
+        for g in range(groups):
+            if b == 3 and g == 1:
+                continue                                  # an empty page list
+            pick = rng.choice(pages, size=min(pages, 60), replace=False)
+            idx[g, b, :len(pick)] = pick
+    args = (to_dev(q), to_dev(inp.k), to_dev(inp.v), cu_dev(cu_q), cu_dev(inp.cu_seqlens), 1,
+            max(cache), to_dev(idx, torch.int32))
+    if splits is None:
+        assert ops.attn_splits(len(cache) * groups, 1, max(cache), 67, DEV) > 1
+    out, lse = ops.sparse_attn(*args, causal=False, return_lse=True, splits=splits)
+    one, lse1 = ops.sparse_attn(*args, causal=False, return_lse=True, splits=1)
+    want, want_lse = ora.sparse_attention(q, inp.k, inp.v, cu_q, inp.cu_seqlens, idx,
+                                          causal=False)
+    _attn_check(out, lse, want, want_lse)
+    assert torch.all(out[3, 16:] == 0) and torch.all(torch.isinf(lse[16:, 3]))
+    # Close to the one-CTA result: each slice rounds its exponentials to bf16
+    # against its own reference max, so the two differ by that rounding, not
+    # by the math.
+    # Per element: one bf16 ulp of the output plus 2e-3.
+    _, e = torch.frexp(one.float().abs())
+    ulp = torch.ldexp(torch.ones_like(one, dtype=torch.float32), e - 8)
+    d = (out.float() - one.float()).abs()
+    assert torch.all(d <= ulp + 2e-3), (d - ulp).max().item()
+    assert d.mean().item() <= 2e-4, d.mean().item()
+    assert ops.check_status(DEV) == 0
+
+
+def test_split_page_lists_keep_the_causal_mask():
+    """A prefill-shaped call forced into slices: each slice masks the keys
+    past its token like the whole list does."""
+    lens = [700, 1300]
+    inp = ora.synthetic_layer(lens, num_heads=32, num_kv_heads=2, head_dim=128, router_heads=4,
+                              router_dim=32, hot_pages=2, seed=85, bf16=True)
+    kc, cu_c = ora.compress_keys(inp.k, inp.cu_seqlens, policy="bf16")
+    sel = ora.lightweight_compressed_attention(inp.q, kc, inp.cu_seqlens, cu_c, inp.params,
+                                               topk=16, init_blocks=1, local_blocks=2,
+                                               policy="bf16")
+    args = (to_dev(inp.q), to_dev(inp.k), to_dev(inp.v), cu_dev(inp.cu_seqlens),
+            cu_dev(inp.cu_seqlens), max(lens), max(lens), to_dev(sel.topk_idx, torch.int32))
+    out, lse = ops.sparse_attn(*args, causal=True, return_lse=True, splits=5)
+    want, want_lse = ora.sparse_attention(inp.q, inp.k, inp.v, inp.cu_seqlens, inp.cu_seqlens,
+                                          sel.topk_idx, causal=True)
+    _attn_check(out, lse, want, want_lse)
+    assert ops.check_status(DEV) == 0
+
+
 def test_sparse_attention_query_chunk_against_key_prefix():
     """Causal, fewer queries than keys: the queries are the last rows of each
     sequence's keys (bottom-right alignment), the form a sequence-parallel rank

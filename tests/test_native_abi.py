@@ -75,6 +75,45 @@ def test_workspace_size_and_check():
     assert b"workspace" in lib.ls_last_error()
 
 
+def test_split_attention_workspace_and_argument_checks():
+    lib = _native.load()
+    # splits x rows x (128 output floats + max + sum) x 4 bytes; nothing for one slice
+    assert lib.ls_sparse_attn_split_workspace_bytes(3, 32, 8) == 8 * 3 * 32 * 130 * 4
+    assert lib.ls_sparse_attn_split_workspace_bytes(3, 32, 1) == 0
+    fake = ctypes.c_void_p(1 << 20)
+    args = (fake, fake, fake, fake, fake, 3, 1, 4096, 3, 3 * 4096, 32, 2, 128, fake, 67, 64, 0.0,
+            0)
+    for splits in (0, _native.LS_MAX_ATTN_SPLITS + 1):
+        rc = lib.ls_sparse_attn_split(*args, splits, fake, 1 << 20, fake, None, None, None)
+        assert rc == _native.LS_ERR_INVALID_ARGUMENT
+        assert b"splits" in lib.ls_last_error()
+    rc = lib.ls_sparse_attn_split(*args, 8, None, 0, fake, None, None, None)
+    assert rc == _native.LS_ERR_INVALID_ARGUMENT
+    rc = lib.ls_sparse_attn_split(*args, 8, fake, 8 * 3 * 32 * 130 * 4 - 1, fake, None, None, None)
+    assert rc == _native.LS_ERR_INVALID_ARGUMENT
+    assert b"workspace" in lib.ls_last_error()
+
+
+def test_split_count_choice():
+    from leanselect_b200 import ops
+
+    class Props:
+        multi_processor_count = 148
+
+    orig = torch.cuda.get_device_properties
+    torch.cuda.get_device_properties = lambda dev: Props()
+    try:
+        dev = torch.device("cpu")
+        assert ops.attn_splits(2, 1, 131072, 67, dev) == 16        # batch 1: pages // 4 caps it
+        assert ops.attn_splits(16, 1, 131072, 67, dev) == 9        # batch 8
+        assert ops.attn_splits(128, 1, 131072, 67, dev) == 1       # batch 64
+        assert ops.attn_splits(1024, 1, 131072, 67, dev) == 1      # enough rows
+        assert ops.attn_splits(2, 1, 200, 67, dev) == 1            # 4 pages: nothing to cut
+        assert ops.attn_splits(2, 4096, 131072, 67, dev) == 1      # prefill is never split
+    finally:
+        torch.cuda.get_device_properties = orig
+
+
 def test_noalloc_checks_arguments_before_its_scratch_limit():
     """A malformed call gets ls_select_pages' own error, not the scratch-size one;
     a well-formed call one token past the 16 MiB limit gets LS_ERR_UNSUPPORTED."""
