@@ -1,12 +1,13 @@
 """Sequence-length sweep of one hot-path layer (benchmark config 3).
 
     python -m measure.sweep [--lengths 32768,65536,131072,262144,524288] [--reps 3]
-                                    [--method leanselect|uniform]
+                                    [--method leanselect|uniform] [--topk 67 --local 2]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
         -m measure.sweep ...            # sequence-parallel over N GPUs
 
 One benchmark config-1 layer (bf16, 32 query / 2 KV heads, head_dim 128,
-budget 64 pages + sink + 2 local pages of 64 tokens) at each length, with
+budget 64 pages + sink + 2 local pages of 64 tokens; ``--topk 96 --local
+32`` is the reference's stock budget, window 2048) at each length, with
 the config-0/1 input distribution: N(0,1) q/k/v, 24 hot pages per KV head
 whose keys (and every query) are shifted by 0.5*u, selector head mix
 N(0, 1/32) over a 32 x 4 router.  Inputs are generated on the device from
@@ -37,12 +38,12 @@ STAGES = ("gather", "compress", "select", "attn")
 
 
 def run_length(n: int, reps: int, device: torch.device, dist=None, seed: int = 0,
-               method: str = "leanselect") -> dict:
+               method: str = "leanselect", topk: int = 67, local: int = 2) -> dict:
     world = dist.get_world_size() if dist is not None else 1
     rank = dist.get_rank() if dist is not None else 0
     if method != "leanselect" and world > 1:
         raise ValueError("the sequence-parallel layer serves the LeanSelect method only")
-    cfg = LayerConfig(topk=67, selection_method=method)
+    cfg = LayerConfig(topk=topk, local_blocks=local, selection_method=method)
     q, k, v = config1_layer(n, device, seed)
     sel = make_selector(device, seed)
     if world > 1:
@@ -87,7 +88,8 @@ def run_length(n: int, reps: int, device: torch.device, dist=None, seed: int = 0
         t = torch.tensor([ms[s] for s in (*STAGES, "total")], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = dict(zip((*STAGES, "total"), t.tolist()))
-    return {"workload": "benchmark config 3: config-1 layer (bf16, 32/2 heads, T=67)",
+    return {"workload": f"benchmark config 3: config-1 layer (bf16, 32/2 heads, T={topk}, "
+                        f"{local} local pages)",
             "method": method, "seq_len": n, "n_gpus": world, "reps": reps, "ms": ms,
             "tokens_per_s": n / (ms["total"] / 1e3),
             "parallelism": f"sp{world}" if world > 1 else "single"}
@@ -100,6 +102,8 @@ def main(argv=None) -> int:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--method", choices=("leanselect", "uniform"), default="leanselect",
                     help="selection method (uniform: the mean-query ablation, one GPU)")
+    ap.add_argument("--topk", type=int, default=67, help="pages per (group, token), T")
+    ap.add_argument("--local", type=int, default=2, help="local pages before the query's own")
     args = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -114,7 +118,8 @@ def main(argv=None) -> int:
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
     try:
         for n in (int(x) for x in args.lengths.split(",")):
-            line = run_length(n, args.reps, device, dist, args.seed, args.method)
+            line = run_length(n, args.reps, device, dist, args.seed, args.method, args.topk,
+                              args.local)
             if dist is None or dist.get_rank() == 0:
                 print(json.dumps(line), flush=True)
             torch.cuda.empty_cache()
