@@ -469,29 +469,40 @@ size_t attn_smem_bytes() { return 1024 + kStages * kStageBytes + 16 * 256 + size
 
 // One warp per (token, head) row: weights each slice's normalised output by
 // its share of the row's softmax mass, l_s * 2^(m_s - max m), and writes the
-// bf16 row (zeros when no slice saw a page) and its log-sum-exp.
+// bf16 row (zeros when no slice saw a page) and its log-sum-exp.  Lane l
+// reads the max and sum of slices l and l + 32 at once; the slices' outputs
+// are then summed with several loads in flight.
 __global__ void __launch_bounds__(256) attn_merge_kernel(const __grid_constant__ AttnArgs args) {
   const int64_t rows = args.total_q * args.num_heads;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (r >= rows) return;
   const int lane = threadIdx.x & 31;
-  float mx = -INFINITY;
-  for (int s = 0; s < args.splits; ++s) {
-    const float2 ml = *reinterpret_cast<const float2*>(args.part_ml + (s * rows + r) * 2);
-    if (ml.y > 0.f) mx = fmaxf(mx, ml.x);
-  }
-  float wsum = 0.f;
+  const int splits = args.splits;  // 2 .. 64
+  float2 ml_a = make_float2(-INFINITY, 0.f), ml_b = make_float2(-INFINITY, 0.f);
+  if (lane < splits) ml_a = *reinterpret_cast<const float2*>(args.part_ml + (lane * rows + r) * 2);
+  if (lane + 32 < splits)
+    ml_b = *reinterpret_cast<const float2*>(args.part_ml + ((lane + 32) * rows + r) * 2);
+  float mx = fmaxf(ml_a.y > 0.f ? ml_a.x : -INFINITY, ml_b.y > 0.f ? ml_b.x : -INFINITY);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float w_a = ml_a.y > 0.f ? ml_a.y * ex2(ml_a.x - mx) : 0.f;
+  const float w_b = ml_b.y > 0.f ? ml_b.y * ex2(ml_b.x - mx) : 0.f;
+  float wsum = w_a + w_b;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s = 0; s < args.splits; ++s) {
-    const float2 ml = *reinterpret_cast<const float2*>(args.part_ml + (s * rows + r) * 2);
-    if (!(ml.y > 0.f)) continue;
-    const float w = ml.y * ex2(ml.x - mx);
-    const float4 o = reinterpret_cast<const float4*>(args.part_o + (s * rows + r) * 128)[lane];
-    wsum += w;
-    acc.x = fmaf(w, o.x, acc.x);
-    acc.y = fmaf(w, o.y, acc.y);
-    acc.z = fmaf(w, o.z, acc.z);
-    acc.w = fmaf(w, o.w, acc.w);
+  const float4* po = reinterpret_cast<const float4*>(args.part_o + r * 128) + lane;
+  const int64_t stride4 = rows * 32;  // float4 per slice
+#pragma unroll 8
+  for (int s = 0; s < splits; ++s) {
+    const float w = __shfl_sync(0xffffffffu, s < 32 ? w_a : w_b, s & 31);
+    if (w > 0.f) {
+      const float4 o = po[s * stride4];
+      acc.x = fmaf(w, o.x, acc.x);
+      acc.y = fmaf(w, o.y, acc.y);
+      acc.z = fmaf(w, o.z, acc.z);
+      acc.w = fmaf(w, o.w, acc.w);
+    }
   }
   const float f = wsum > 0.f ? 1.f / wsum : 0.f;
   uint2 packed;
@@ -505,6 +516,7 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(const __grid_constant__
         wsum > 0.f ? (mx + __log2f(wsum)) * 0.69314718055994531f : INFINITY;
   }
 }
+
 
 }  // namespace
 

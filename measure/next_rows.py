@@ -13,7 +13,10 @@ Seeded synthetic inputs (the benchmark layer's distribution); CUDA events on
 the launching stream, median of ``--reps``; the L2 is flushed (a 256 MB
 write) before every timed call, so each call reads its inputs from HBM.
 
-Usage: ``python -m measure.next_rows [--reps 10]``
+Usage: ``python -m measure.next_rows [--reps 10] [--small]``
+
+``--small`` runs each call once on reduced sizes (f1 at 32K keys, f2 at 8K
+tokens, f4 at batch 1 on 32K caches): the workload for profiler captures.
 """
 from __future__ import annotations
 
@@ -56,7 +59,10 @@ def peaks():
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--small", action="store_true", help="one call each, reduced sizes")
     args = ap.parse_args(argv)
+    if args.small:
+        return small()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=DEV)
     hbm, hbm_kind = peaks()
 
@@ -142,6 +148,35 @@ def main(argv=None) -> int:
                           "hbm_frac": gathered / t_split / 1e6 / hbm}), flush=True)
         del kk, vv
     assert ops.check_status(DEV) == 0
+    return 0
+
+
+def small() -> int:
+    """One call of each kernel on reduced inputs (for profiler captures)."""
+    n = 32768
+    _, k, _ = config1_layer(n, DEV, 0)
+    cu = torch.tensor([0, n], dtype=torch.int32, device=DEV)
+    ops.compress_keys_dual(k, cu, lengths=[n])
+    n2 = 8192
+    q2, k2, _ = config1_layer(n2, DEV, 1)
+    cu2 = torch.tensor([0, n2], dtype=torch.int32, device=DEV)
+    w = make_selector(DEV, 1).kernel_weights()
+    kc2, cu_c2 = ops.compress_keys(k2, cu2, lengths=[n2])
+    ks2 = ops.project_atom_keys(kc2, w.wk_t)
+    ops.atom_scores(q2, w, ks2, cu2, cu_c2, n2, kc2.shape[0])
+    cache = 32768
+    gen = torch.Generator(device="cpu").manual_seed(7)
+    kk = torch.randn(cache, 2, 128, device=DEV, dtype=torch.bfloat16)
+    vv = torch.randn_like(kk)
+    qq = torch.randn(1, 32, 128, device=DEV, dtype=torch.bfloat16)
+    idx = torch.stack([torch.randperm(cache // 64, generator=gen)[:67] for _ in range(2)])
+    idx = idx.view(2, 1, 67).to(torch.int32).to(DEV)
+    cu_q = torch.tensor([0, 1], dtype=torch.int32, device=DEV)
+    cu_k = torch.tensor([0, cache], dtype=torch.int32, device=DEV)
+    ops.sparse_attn(qq, kk, vv, cu_q, cu_k, 1, cache, idx, causal=False)
+    torch.cuda.synchronize()
+    assert ops.check_status(DEV) == 0
+    print("next_rows small ok", flush=True)
     return 0
 
 
