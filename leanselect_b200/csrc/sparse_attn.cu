@@ -16,7 +16,10 @@
 //               keeps its own online softmax (m, l, O[16 x 128] in registers);
 //               the four partial results are merged at the end.
 // The page list is loaded once, invalid entries dropped, sorted and
-// de-duplicated by one warp (bitonic network over 128 slots).
+// de-duplicated by one warp (bitonic network over 128 slots; a list that is
+// already strictly ascending, as the selection kernels write it, is not
+// sorted).  Its loads and the Q rows' are issued before anything else in the
+// CTA, so their latency overlaps the sequence lookup.
 #include "common.cuh"
 #include "launch.h"
 
@@ -128,6 +131,26 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
   const int64_t t = group_major ? item % args.total_q : item / args.num_groups;
   const int g = group_major ? static_cast<int>(item / args.total_q)
                             : static_cast<int>(item % args.num_groups);
+  // The page list and the Q rows depend only on (t, g): their loads are
+  // issued first, so their latency overlaps the sequence lookup below.
+  int32_t praw[4];
+  uint4 qraw[8];
+  if (warp == 0) {
+    const int32_t* row = args.topk_idx + (static_cast<int64_t>(g) * args.total_q + t) * args.topk;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int pos = 32 * r + lane;
+      praw[r] = pos < args.topk ? __ldg(row + pos) : -1;
+    }
+  } else if (warp == 1) {
+    const uint4* src = reinterpret_cast<const uint4*>(args.q + (t * args.num_heads + g * HG) * 128);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = lane + 32 * k;
+      const int r = i >> 4, c = i & 15;
+      qraw[k] = r < HG ? __ldg(src + r * 16 + c) : make_uint4(0, 0, 0, 0);
+    }
+  }
   const int b = find_sequence(args.cu_q, args.batch, t);
   const int64_t q_start = __ldg(args.cu_q + b);
   const int64_t k_start = __ldg(args.cu_k + b);
@@ -149,17 +172,25 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
   if (warp == 0) {
     // Page list: drop empty/out-of-range/fully-masked entries, sort, de-duplicate.
     int32_t v[4];
-    const int32_t* row = args.topk_idx + (static_cast<int64_t>(g) * args.total_q + t) * args.topk;
     bool bad_index = false;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      const int pos = 32 * r + lane;
-      int32_t p = pos < args.topk ? __ldg(row + pos) : -1;
+      const int32_t p = praw[r];
       if (p >= n_kpages) bad_index = true;
       v[r] = (p >= 0 && p < n_kpages && p * 64 <= t_lim) ? p : kSentinel;
     }
     if (__any_sync(0xffffffffu, bad_index) && lane == 0) report(args.status, LS_DEVERR_PAGE_INDEX);
-    warp_bitonic_sort128(v, lane);
+    // Strictly ascending valid entries followed by sentinels (the lists the
+    // selection kernels write) need no sort.
+    bool ordered = true;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      int32_t next = __shfl_down_sync(0xffffffffu, v[r], 1);
+      const int32_t next_row = __shfl_sync(0xffffffffu, v[r < 3 ? r + 1 : r], 0);
+      if (lane == 31) next = r < 3 ? next_row : kSentinel;
+      ordered = ordered && (v[r] < next || next == kSentinel);
+    }
+    if (!__all_sync(0xffffffffu, ordered)) warp_bitonic_sort128(v, lane);
     int base = 0;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
@@ -174,12 +205,11 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attn_kernel(const __grid_c
     if (lane == 0) sm->n_pages = base;
   } else if (warp == 1) {
     // Q rows of this group (HG heads, padded to 16 rows with zeros), swizzled.
-    const uint4* src = reinterpret_cast<const uint4*>(args.q + (t * args.num_heads + g * HG) * 128);
-    for (int i = lane; i < 16 * 16; i += 32) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = lane + 32 * k;
       const int r = i >> 4, c = i & 15;
-      uint4 val = make_uint4(0, 0, 0, 0);
-      if (r < HG) val = __ldg(src + r * 16 + c);
-      *reinterpret_cast<uint4*>(q_smem + r * 256 + (((c & 7) ^ (r & 7)) | (c & 8)) * 16) = val;
+      *reinterpret_cast<uint4*>(q_smem + r * 256 + (((c & 7) ^ (r & 7)) | (c & 8)) * 16) = qraw[k];
     }
   }
   __syncthreads();
