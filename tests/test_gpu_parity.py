@@ -601,8 +601,9 @@ def test_decode_step_through_sparse_forward_contract():
     assert ops.check_status(DEV) == 0
 
 
+@pytest.mark.parametrize("heads", [(32, 2), (16, 2)])
 @pytest.mark.parametrize("splits", [None, 2, 7, 64])
-def test_decode_attention_with_split_page_lists(splits):
+def test_decode_attention_with_split_page_lists(splits, heads):
     """Decode rows with their page lists cut into slices (``ls_sparse_attn_split``,
     chosen automatically for decode calls): the slices' partial results,
     combined by their share of each row's exponential mass, give the oracle's
@@ -610,7 +611,7 @@ def test_decode_attention_with_split_page_lists(splits):
     (empty slices), for a row whose list is all -1 (zeros, lse +inf), and
     within fp32 summation order of the one-CTA-per-row kernel."""
     cache = [4096, 64, 777, 131, 2500]
-    heads, groups = 32, 2
+    heads, groups = heads
     inp = ora.synthetic_layer(cache, num_heads=heads, num_kv_heads=groups, head_dim=128,
                               router_heads=4, router_dim=32, hot_pages=2, seed=83, bf16=True)
     last = inp.cu_seqlens[1:] - 1
@@ -634,7 +635,8 @@ def test_decode_attention_with_split_page_lists(splits):
     want, want_lse = ora.sparse_attention(q, inp.k, inp.v, cu_q, inp.cu_seqlens, idx,
                                           causal=False)
     _attn_check(out, lse, want, want_lse)
-    assert torch.all(out[3, 16:] == 0) and torch.all(torch.isinf(lse[16:, 3]))
+    hg = heads // groups
+    assert torch.all(out[3, hg:] == 0) and torch.all(torch.isinf(lse[hg:, 3]))
     # Close to the one-CTA result: each slice rounds its exponentials to bf16
     # against its own reference max, so the two differ by that rounding, not
     # by the math.
