@@ -1,12 +1,13 @@
 // Block-sparse causal attention over per-token page lists (stage 2, a9).
 //
 // Replaces infllmv2_attn_varlen_func(..., topk_idx=) (minicpm.py:3229-3243).
-// LeanSelect picks pages per query token, and on the benchmark inputs the
-// lists of neighbouring tokens barely overlap, so a tensor-core tile that
-// spans several tokens would compute mostly masked products.  This kernel
-// therefore works per (token, KV group): the Hg query heads of the group form
-// the 16 rows of an m16n8k16 tile and the keys of the token's own pages form
-// the columns, so every product computed is a product the token needs.
+// LeanSelect picks pages per query token, and on the benchmark inputs a
+// page shared by 8 neighbouring tokens is read by only 1.4 of them on
+// average, so a tensor-core tile that spans several tokens would compute
+// mostly masked products.  This kernel therefore works per (token, KV
+// group): the Hg query heads of the group form the 16 rows of an m16n8k16
+// tile and the keys of the token's own pages form the columns, so every
+// product computed is a product the token needs.
 //
 // CTA = one (packed token, group); 5 warps:
 //   warp 4      TMA producer: streams each selected page's K and V
@@ -20,6 +21,10 @@
 // already strictly ascending, as the selection kernels write it, is not
 // sorted).  Its loads and the Q rows' are issued before anything else in the
 // CTA, so their latency overlaps the sequence lookup.
+//
+// For few query rows (a decode step) the page list of each row can be cut
+// into `splits` slices, one CTA each (AttnArgs::splits); the slices write
+// partial results that attn_merge_kernel combines.
 #include "common.cuh"
 #include "launch.h"
 
