@@ -38,7 +38,7 @@ METRIC = "prefill tokens/sec @128K (8B shape); select+attn ms/layer"
 # DRAM bytes (read + write) of one sparse-attention launch at 131072 tokens,
 # from a committed ncu capture: ncu cannot run inside the timed bench, and a
 # multi-pass capture of the 32-layer model would not fit the profiling rules.
-ATTN_TRAFFIC_BYTES = 6756.5e6 + 1070.9e6
+ATTN_TRAFFIC_BYTES = 6750.0e6 + 1070.8e6
 ATTN_TRAFFIC_SOURCE = (
     "ncu dram__bytes_read.sum + dram__bytes_write.sum of sparse_attn_kernel<16> at 131072 tokens "
     "(python -m measure.profile_case --seq-len 131072, the config-1 layer: same kernel, length "
